@@ -1,0 +1,472 @@
+// skv_abi.cu - the extern "C" surface of libstrata_kv.so (declared in include/strata_kv.h).
+//
+// Host-side glue only: argument checks (refusals happen here, before anything is enqueued, the way the
+// reference validates before its first write - include/strata/core/conversation_snapshot.hpp:103-108),
+// the block pool and its allocator, plan building for the copy kernels in skv_copy.cu, pinned host
+// memory, peer access / CUDA IPC and the completion flags.
+#include "skv_internal.h"
+
+#include <algorithm>
+#include <cstdio>
+#include <cstring>
+#include <memory>
+#include <mutex>
+#include <vector>
+
+namespace skv {
+
+namespace {
+thread_local std::string t_error;
+std::mutex g_ctx_mu;
+std::vector<std::unique_ptr<DeviceCtx>> g_ctx;   // indexed by device ordinal
+
+uint64_t splitmix64(uint64_t x) {
+    x += 0x9E3779B97F4A7C15ull;
+    x = (x ^ (x >> 30)) * 0xBF58476D1CE4E5B9ull;
+    x = (x ^ (x >> 27)) * 0x94D049BB133111EBull;
+    return x ^ (x >> 31);
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+}  // namespace
+
+void set_error(const std::string& message) { t_error = message; }
+
+int fail(int code, const std::string& message) {
+    t_error = message;
+    return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+    t_error = std::string(what) + ": " + cudaGetErrorString(e);
+    return SKV_ECUDA;
+}
+
+DeviceCtx* current_ctx() {
+    int dev = -1;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) {
+        cuda_fail(e, "cudaGetDevice");
+        return nullptr;
+    }
+    std::lock_guard<std::mutex> lock(g_ctx_mu);
+    if ((size_t) dev >= g_ctx.size()) g_ctx.resize((size_t) dev + 1);
+    if (g_ctx[(size_t) dev]) return g_ctx[(size_t) dev].get();
+    auto ctx = std::make_unique<DeviceCtx>();
+    ctx->device = dev;
+    e = cudaDeviceGetAttribute(&ctx->sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) {
+        cuda_fail(e, "cudaDeviceGetAttribute(SM count)");
+        return nullptr;
+    }
+    e = cudaMalloc(&ctx->status, 256);
+    if (e == cudaSuccess) e = cudaMemset(ctx->status, 0, 256);
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) {
+        cuda_fail(e, "device status word");
+        return nullptr;
+    }
+    g_ctx[(size_t) dev] = std::move(ctx);
+    return g_ctx[(size_t) dev].get();
+}
+
+/// Validate the public segments and turn them into a kernel plan.  Zero-byte segments are dropped.
+static int build_plan(const skv_segment* segs, int n_segs, int engine, CopyPlan& plan, uint64_t& total_tiles) {
+    if (n_segs < 0 || n_segs > SKV_COPY_MAX_SEGMENTS || (n_segs && !segs))
+        return fail(SKV_EINVAL, "skv_copy: segment count must be in [0, SKV_COPY_MAX_SEGMENTS]");
+    if (engine != SKV_COPY_TMA && engine != SKV_COPY_VEC) return fail(SKV_EINVAL, "skv_copy: unknown copy engine");
+    std::memset(&plan, 0, sizeof plan);
+    total_tiles = 0;
+    int k = 0;
+    for (int i = 0; i < n_segs; ++i) {
+        const skv_segment& s = segs[i];
+        if (s.bytes == 0) continue;
+        char where[96];
+        std::snprintf(where, sizeof where, "skv_copy: segment %d: ", i);
+        if (!s.src || !s.dst) return fail(SKV_EINVAL, std::string(where) + "missing buffer");
+        if (!aligned16(s.src) || !aligned16(s.dst) || s.bytes % 16)
+            return fail(SKV_EINVAL, std::string(where) + "buffers must be 16-byte aligned and bytes a multiple of 16");
+        const bool paged = s.src_pages || s.dst_pages;
+        SegDev d{};
+        d.src = static_cast<const uint8_t*>(s.src);
+        d.dst = static_cast<uint8_t*>(s.dst);
+        d.src_pages = s.src_pages;
+        d.dst_pages = s.dst_pages;
+        d.bytes = s.bytes;
+        d.src_page_limit = s.src_page_limit;
+        d.dst_page_limit = s.dst_page_limit;
+        if (paged) {
+            if (s.page_bytes == 0 || s.page_bytes % 16 || s.bytes % s.page_bytes)
+                return fail(SKV_EINVAL, std::string(where) + "a paged side needs page_bytes a multiple of 16 dividing bytes");
+            if ((s.src_pages && s.src_page_limit <= 0) || (s.dst_pages && s.dst_page_limit <= 0))
+                return fail(SKV_EINVAL, std::string(where) + "a paged side needs a positive page limit");
+            d.page_bytes = s.page_bytes;
+            if (engine == SKV_COPY_TMA) {
+                if (s.page_bytes < 1024 || s.page_bytes > kTmaTileBytes)
+                    return fail(SKV_EINVAL, std::string(where) + "the TMA engine stages pages of 1 KiB to 32 KiB");
+                d.pages_per_tile = std::min<uint32_t>(32u, kTmaTileBytes / s.page_bytes);
+            } else {
+                d.pages_per_tile = std::max<uint32_t>(1u, std::min<uint32_t>(512u, kVecTileBytes / s.page_bytes));
+            }
+            d.tile_bytes = (uint64_t) d.pages_per_tile * s.page_bytes;
+        } else {
+            d.tile_bytes = engine == SKV_COPY_TMA ? kTmaTileBytes : kVecTileBytes;
+        }
+        total_tiles += (d.bytes + d.tile_bytes - 1) / d.tile_bytes;
+        plan.seg[k] = d;
+        plan.tile_end[k] = total_tiles;
+        ++k;
+    }
+    plan.n_segs = k;
+    return SKV_OK;
+}
+
+/// AUTO: the bulk engine when every buffer is this device's own memory and every page granule suits it.
+static int pick_engine(const skv_segment* segs, int n_segs, int device) {
+    for (int i = 0; i < n_segs; ++i) {
+        const skv_segment& s = segs[i];
+        if (s.bytes == 0) continue;
+        if ((s.src_pages || s.dst_pages) && (s.page_bytes < 1024 || s.page_bytes > kTmaTileBytes)) return SKV_COPY_VEC;
+        for (const void* p : {s.src, static_cast<const void*>(s.dst)}) {
+            cudaPointerAttributes a{};
+            if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+                (void) cudaGetLastError();
+                return SKV_COPY_VEC;
+            }
+            if (a.type != cudaMemoryTypeDevice || a.device != device) return SKV_COPY_VEC;
+        }
+    }
+    return SKV_COPY_TMA;
+}
+
+}  // namespace skv
+
+using namespace skv;
+
+// ====================================================================== extern "C"
+
+struct skv_pool {
+    int device = -1;
+    bool owned = true;
+    void* base = nullptr;
+    uint64_t block_bytes = 0;
+    int64_t n_blocks = 0;
+    std::vector<int32_t> free_list;   // popped from the back
+    std::vector<uint8_t> used;
+    std::mutex mu;
+};
+
+extern "C" {
+
+const char* skv_last_error(void) { return t_error.c_str(); }
+
+int skv_version(void) { return 1; }
+
+int skv_pool_create(int device, int64_t n_blocks, uint64_t block_bytes, skv_pool** out) {
+    if (!out) return fail(SKV_EINVAL, "skv_pool_create: null output");
+    *out = nullptr;
+    if (n_blocks <= 0 || n_blocks > INT32_MAX || block_bytes == 0 || block_bytes % 1024)
+        return fail(SKV_EINVAL, "skv_pool_create: n_blocks in [1, 2^31) and block_bytes a positive multiple of 1 KiB");
+    if ((uint64_t) n_blocks > UINT64_MAX / block_bytes) return fail(SKV_ERANGE, "skv_pool_create: pool size overflows");
+    int prev = -1;
+    cudaError_t e = cudaGetDevice(&prev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+    if ((e = cudaSetDevice(device)) != cudaSuccess) return cuda_fail(e, "cudaSetDevice");
+    auto pool = std::make_unique<skv_pool>();
+    pool->device = device;
+    pool->block_bytes = block_bytes;
+    pool->n_blocks = n_blocks;
+    e = cudaMalloc(&pool->base, (size_t) n_blocks * block_bytes);
+    cudaSetDevice(prev);
+    if (e != cudaSuccess) {
+        (void) cudaGetLastError();
+        return fail(SKV_ENOMEM, std::string("skv_pool_create: cudaMalloc: ") + cudaGetErrorString(e));
+    }
+    pool->free_list.resize((size_t) n_blocks);
+    for (int64_t i = 0; i < n_blocks; ++i) pool->free_list[(size_t) i] = (int32_t) (n_blocks - 1 - i);
+    pool->used.assign((size_t) n_blocks, 0);
+    *out = pool.release();
+    return SKV_OK;
+}
+
+int skv_pool_wrap(int device, void* base, int64_t n_blocks, uint64_t block_bytes, skv_pool** out) {
+    if (!out) return fail(SKV_EINVAL, "skv_pool_wrap: null output");
+    *out = nullptr;
+    if (!base || (reinterpret_cast<uintptr_t>(base) & 255u) || n_blocks <= 0 || n_blocks > INT32_MAX ||
+        block_bytes == 0 || block_bytes % 1024)
+        return fail(SKV_EINVAL, "skv_pool_wrap: a 256-byte aligned base, n_blocks in [1, 2^31), block_bytes a multiple of 1 KiB");
+    auto pool = std::make_unique<skv_pool>();
+    pool->device = device;
+    pool->owned = false;
+    pool->base = base;
+    pool->block_bytes = block_bytes;
+    pool->n_blocks = n_blocks;
+    pool->free_list.resize((size_t) n_blocks);
+    for (int64_t i = 0; i < n_blocks; ++i) pool->free_list[(size_t) i] = (int32_t) (n_blocks - 1 - i);
+    pool->used.assign((size_t) n_blocks, 0);
+    *out = pool.release();
+    return SKV_OK;
+}
+
+int skv_pool_destroy(skv_pool* pool) {
+    if (!pool) return SKV_OK;
+    if (!pool->owned) {
+        delete pool;
+        return SKV_OK;
+    }
+    int prev = -1;
+    cudaGetDevice(&prev);
+    cudaSetDevice(pool->device);
+    const cudaError_t e = cudaFree(pool->base);
+    cudaSetDevice(prev);
+    delete pool;
+    return e == cudaSuccess ? SKV_OK : cuda_fail(e, "skv_pool_destroy: cudaFree");
+}
+
+void* skv_pool_base(const skv_pool* pool) { return pool ? pool->base : nullptr; }
+uint64_t skv_pool_block_bytes(const skv_pool* pool) { return pool ? pool->block_bytes : 0; }
+int64_t skv_pool_blocks(const skv_pool* pool) { return pool ? pool->n_blocks : 0; }
+int skv_pool_device(const skv_pool* pool) { return pool ? pool->device : -1; }
+
+int skv_alloc_blocks(skv_pool* pool, int64_t n, int32_t* out_ids) {
+    if (!pool || n < 0 || (n && !out_ids)) return fail(SKV_EINVAL, "skv_alloc_blocks: bad arguments");
+    std::lock_guard<std::mutex> lock(pool->mu);
+    if ((uint64_t) n > pool->free_list.size()) return fail(SKV_ENOMEM, "skv_alloc_blocks: the pool has too few free blocks");
+    for (int64_t i = 0; i < n; ++i) {
+        const int32_t id = pool->free_list.back();
+        pool->free_list.pop_back();
+        pool->used[(size_t) id] = 1;
+        out_ids[i] = id;
+    }
+    return SKV_OK;
+}
+
+int skv_free_blocks(skv_pool* pool, const int32_t* ids, int64_t n) {
+    if (!pool || n < 0 || (n && !ids)) return fail(SKV_EINVAL, "skv_free_blocks: bad arguments");
+    std::lock_guard<std::mutex> lock(pool->mu);
+    // validate all first: a double free or a foreign id frees nothing
+    std::vector<uint8_t> seen;
+    for (int64_t i = 0; i < n; ++i) {
+        const int32_t id = ids[i];
+        if (id < 0 || id >= pool->n_blocks || !pool->used[(size_t) id])
+            return fail(SKV_EINVAL, "skv_free_blocks: block " + std::to_string(id) + " is not allocated");
+        if (seen.empty()) seen.assign((size_t) pool->n_blocks, 0);
+        if (seen[(size_t) id]++) return fail(SKV_EINVAL, "skv_free_blocks: block " + std::to_string(id) + " listed twice");
+    }
+    for (int64_t i = 0; i < n; ++i) {
+        pool->used[(size_t) ids[i]] = 0;
+        pool->free_list.push_back(ids[i]);
+    }
+    return SKV_OK;
+}
+
+int64_t skv_pool_free_count(const skv_pool* pool) {
+    if (!pool) return -1;
+    std::lock_guard<std::mutex> lock(const_cast<skv_pool*>(pool)->mu);
+    return (int64_t) pool->free_list.size();
+}
+
+int skv_pool_scramble(skv_pool* pool, uint64_t seed) {
+    if (!pool) return fail(SKV_EINVAL, "skv_pool_scramble: null pool");
+    std::lock_guard<std::mutex> lock(pool->mu);
+    uint64_t state = splitmix64(seed ^ 0xBB67AE8584CAA73Bull);
+    auto& f = pool->free_list;
+    for (size_t i = f.size(); i > 1; --i) {
+        state = splitmix64(state);
+        std::swap(f[i - 1], f[(size_t) (state % i)]);
+    }
+    return SKV_OK;
+}
+
+int skv_expand_block_table(const int32_t* block_table, int64_t n_blocks, int64_t pages_per_block, int64_t slot_pages,
+                           int64_t page_offset, int32_t* page_table) {
+    if (n_blocks < 0 || pages_per_block <= 0 || slot_pages < pages_per_block || page_offset < 0 ||
+        page_offset + pages_per_block > slot_pages || (n_blocks && (!block_table || !page_table)))
+        return fail(SKV_EINVAL, "skv_expand_block_table: bad arguments");
+    for (int64_t b = 0; b < n_blocks; ++b) {
+        const int64_t base = (int64_t) block_table[b] * slot_pages + page_offset;
+        if (block_table[b] < 0 || base + pages_per_block - 1 > INT32_MAX)
+            return fail(SKV_ERANGE, "skv_expand_block_table: page index outside int32");
+        for (int64_t j = 0; j < pages_per_block; ++j) page_table[b * pages_per_block + j] = (int32_t) (base + j);
+    }
+    return SKV_OK;
+}
+
+int skv_copy(const skv_segment* segs, int n_segs, int engine, void* stream) {
+    DeviceCtx* ctx = current_ctx();
+    if (!ctx) return SKV_ECUDA;
+    if (engine == SKV_COPY_AUTO) engine = pick_engine(segs, n_segs, ctx->device);
+    CopyPlan plan;
+    uint64_t tiles = 0;
+    if (const int rc = build_plan(segs, n_segs, engine, plan, tiles)) return rc;
+    plan.status = ctx->status;
+    return launch_copy(plan, tiles, engine, *ctx, static_cast<cudaStream_t>(stream));
+}
+
+int skv_query_status(int device, void* stream, uint32_t* out_status) {
+    if (!out_status) return fail(SKV_EINVAL, "skv_query_status: null output");
+    int prev = -1;
+    cudaGetDevice(&prev);
+    cudaSetDevice(device);
+    DeviceCtx* ctx = current_ctx();
+    int rc = SKV_OK;
+    if (!ctx) rc = SKV_ECUDA;
+    else {
+        cudaError_t e = cudaMemcpyAsync(out_status, ctx->status, 4, cudaMemcpyDeviceToHost, static_cast<cudaStream_t>(stream));
+        if (e == cudaSuccess) e = cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
+        if (e != cudaSuccess) rc = cuda_fail(e, "skv_query_status");
+    }
+    cudaSetDevice(prev);
+    return rc;
+}
+
+int skv_clear_status(int device, void* stream) {
+    int prev = -1;
+    cudaGetDevice(&prev);
+    cudaSetDevice(device);
+    DeviceCtx* ctx = current_ctx();
+    int rc = SKV_OK;
+    if (!ctx) rc = SKV_ECUDA;
+    else {
+        const cudaError_t e = cudaMemsetAsync(ctx->status, 0, 4, static_cast<cudaStream_t>(stream));
+        if (e != cudaSuccess) rc = cuda_fail(e, "skv_clear_status");
+    }
+    cudaSetDevice(prev);
+    return rc;
+}
+
+int skv_host_alloc(uint64_t bytes, void** out) {
+    if (!out) return fail(SKV_EINVAL, "skv_host_alloc: null output");
+    *out = nullptr;
+    if (bytes == 0) return SKV_OK;
+    const cudaError_t e = cudaHostAlloc(out, bytes, cudaHostAllocPortable | cudaHostAllocMapped);
+    if (e != cudaSuccess) {
+        (void) cudaGetLastError();
+        return fail(SKV_ENOMEM, std::string("skv_host_alloc: ") + cudaGetErrorString(e));
+    }
+    return SKV_OK;
+}
+
+int skv_host_free(void* p) {
+    if (!p) return SKV_OK;
+    const cudaError_t e = cudaFreeHost(p);
+    return e == cudaSuccess ? SKV_OK : cuda_fail(e, "skv_host_free");
+}
+
+/// STAGED transfers: the staging layout is the segments' bytes back to back, each 256-byte aligned.
+static int staged_offsets(const skv_segment* segs, int n, uint64_t staging_bytes, std::vector<uint64_t>& off) {
+    off.assign((size_t) n, 0);
+    uint64_t at = 0;
+    for (int i = 0; i < n; ++i) {
+        off[(size_t) i] = at;
+        at += (segs[i].bytes + 255) & ~255ull;
+    }
+    if (at > staging_bytes) return fail(SKV_ERANGE, "skv_park/resume: staging buffer smaller than the segments");
+    return SKV_OK;
+}
+
+int skv_park(const skv_segment* segs, int n_segs, int mode, void* staging, uint64_t staging_bytes, void* stream) {
+    if (mode == SKV_PARK_DIRECT) return skv_copy(segs, n_segs, SKV_COPY_VEC, stream);
+    if (mode != SKV_PARK_STAGED) return fail(SKV_EINVAL, "skv_park: unknown mode");
+    if (n_segs < 0 || n_segs > SKV_COPY_MAX_SEGMENTS || (n_segs && !segs) || !staging)
+        return fail(SKV_EINVAL, "skv_park: bad arguments");
+    std::vector<uint64_t> off;
+    if (const int rc = staged_offsets(segs, n_segs, staging_bytes, off)) return rc;
+    std::vector<skv_segment> gather(segs, segs + n_segs);
+    for (int i = 0; i < n_segs; ++i) {
+        if (segs[i].dst_pages) return fail(SKV_EINVAL, "skv_park: a staged park needs contiguous host destinations");
+        gather[(size_t) i].dst = static_cast<uint8_t*>(staging) + off[(size_t) i];
+        gather[(size_t) i].dst_pages = nullptr;
+    }
+    if (const int rc = skv_copy(gather.data(), n_segs, SKV_COPY_AUTO, stream)) return rc;
+    for (int i = 0; i < n_segs; ++i) {
+        if (!segs[i].bytes) continue;
+        const cudaError_t e = cudaMemcpyAsync(segs[i].dst, static_cast<uint8_t*>(staging) + off[(size_t) i], segs[i].bytes,
+                                              cudaMemcpyDeviceToHost, static_cast<cudaStream_t>(stream));
+        if (e != cudaSuccess) return cuda_fail(e, "skv_park: cudaMemcpyAsync");
+    }
+    return SKV_OK;
+}
+
+int skv_resume(const skv_segment* segs, int n_segs, int mode, void* staging, uint64_t staging_bytes, void* stream) {
+    if (mode == SKV_PARK_DIRECT) return skv_copy(segs, n_segs, SKV_COPY_VEC, stream);
+    if (mode != SKV_PARK_STAGED) return fail(SKV_EINVAL, "skv_resume: unknown mode");
+    if (n_segs < 0 || n_segs > SKV_COPY_MAX_SEGMENTS || (n_segs && !segs) || !staging)
+        return fail(SKV_EINVAL, "skv_resume: bad arguments");
+    std::vector<uint64_t> off;
+    if (const int rc = staged_offsets(segs, n_segs, staging_bytes, off)) return rc;
+    std::vector<skv_segment> scatter(segs, segs + n_segs);
+    for (int i = 0; i < n_segs; ++i) {
+        if (segs[i].src_pages) return fail(SKV_EINVAL, "skv_resume: a staged resume needs contiguous host sources");
+        if (!segs[i].bytes) continue;
+        const cudaError_t e = cudaMemcpyAsync(static_cast<uint8_t*>(staging) + off[(size_t) i], segs[i].src, segs[i].bytes,
+                                              cudaMemcpyHostToDevice, static_cast<cudaStream_t>(stream));
+        if (e != cudaSuccess) return cuda_fail(e, "skv_resume: cudaMemcpyAsync");
+        scatter[(size_t) i].src = static_cast<uint8_t*>(staging) + off[(size_t) i];
+    }
+    return skv_copy(scatter.data(), n_segs, SKV_COPY_AUTO, stream);
+}
+
+int skv_enable_peer(int device, int peer) {
+    if (device == peer) return SKV_OK;
+    int can = 0;
+    cudaError_t e = cudaDeviceCanAccessPeer(&can, device, peer);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceCanAccessPeer");
+    if (!can) return fail(SKV_EINVAL, "skv_enable_peer: the devices cannot access each other");
+    int prev = -1;
+    cudaGetDevice(&prev);
+    cudaSetDevice(device);
+    e = cudaDeviceEnablePeerAccess(peer, 0);
+    cudaSetDevice(prev);
+    if (e == cudaErrorPeerAccessAlreadyEnabled) {
+        (void) cudaGetLastError();
+        return SKV_OK;
+    }
+    return e == cudaSuccess ? SKV_OK : cuda_fail(e, "cudaDeviceEnablePeerAccess");
+}
+
+int skv_ipc_export(void* dev_ptr, uint8_t handle[64]) {
+    if (!dev_ptr || !handle) return fail(SKV_EINVAL, "skv_ipc_export: bad arguments");
+    static_assert(sizeof(cudaIpcMemHandle_t) == 64, "CUDA IPC handles are 64 bytes");
+    cudaIpcMemHandle_t h;
+    const cudaError_t e = cudaIpcGetMemHandle(&h, dev_ptr);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaIpcGetMemHandle");
+    std::memcpy(handle, &h, 64);
+    return SKV_OK;
+}
+
+int skv_ipc_import(int device, const uint8_t handle[64], void** out_ptr) {
+    if (!handle || !out_ptr) return fail(SKV_EINVAL, "skv_ipc_import: bad arguments");
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, handle, 64);
+    int prev = -1;
+    cudaGetDevice(&prev);
+    cudaSetDevice(device);
+    const cudaError_t e = cudaIpcOpenMemHandle(out_ptr, h, cudaIpcMemLazyEnablePeerAccess);
+    cudaSetDevice(prev);
+    return e == cudaSuccess ? SKV_OK : cuda_fail(e, "cudaIpcOpenMemHandle");
+}
+
+int skv_ipc_close(void* ptr) {
+    if (!ptr) return SKV_OK;
+    const cudaError_t e = cudaIpcCloseMemHandle(ptr);
+    return e == cudaSuccess ? SKV_OK : cuda_fail(e, "cudaIpcCloseMemHandle");
+}
+
+int skv_signal(uint64_t* flag, uint64_t value, void* stream) {
+    if (!flag || (reinterpret_cast<uintptr_t>(flag) & 7u))
+        return fail(SKV_EINVAL, "skv_signal: the flag must be an 8-byte aligned device address");
+    return launch_signal(flag, value, static_cast<cudaStream_t>(stream));
+}
+
+int skv_wait_flag(const uint64_t* flag, uint64_t value, uint64_t timeout_ns, void* stream) {
+    if (!flag || (reinterpret_cast<uintptr_t>(flag) & 7u))
+        return fail(SKV_EINVAL, "skv_wait_flag: the flag must be an 8-byte aligned device address");
+    if (timeout_ns == 0 || timeout_ns > 60ull * 1000000000ull)
+        return fail(SKV_EINVAL, "skv_wait_flag: timeout must be in (0, 60 s]");
+    DeviceCtx* ctx = current_ctx();
+    if (!ctx) return SKV_ECUDA;
+    return launch_wait(flag, value, timeout_ns, ctx->status, static_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

@@ -1,0 +1,63 @@
+// skv_internal.h - shared declarations between the kernel file and the C-ABI glue of libstrata_kv.so.
+#pragma once
+
+#include "strata_kv.h"
+
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <string>
+
+namespace skv {
+
+/// One segment as the kernels see it: the public skv_segment plus its tiling.
+struct SegDev {
+    const uint8_t* src;
+    uint8_t* dst;
+    const int32_t* src_pages;
+    const int32_t* dst_pages;
+    uint64_t bytes;
+    uint64_t tile_bytes;      // bytes per tile (whole pages when either side is paged)
+    uint32_t page_bytes;      // 0 when both sides are contiguous
+    uint32_t pages_per_tile;  // 0 when both sides are contiguous
+    int64_t src_page_limit;
+    int64_t dst_page_limit;
+};
+
+/// The whole launch: passed by value as a __grid_constant__ kernel parameter (no device allocation, no
+/// H2D copy, capturable in a CUDA graph).
+struct CopyPlan {
+    int n_segs;
+    int pad;
+    uint32_t* status;                           // the device status word (SKV_STATUS_* bits)
+    uint64_t tile_end[SKV_COPY_MAX_SEGMENTS];   // inclusive prefix sum of tiles per segment
+    SegDev seg[SKV_COPY_MAX_SEGMENTS];
+};
+
+/// TMA engine geometry: a ring of kTmaStages tiles of kTmaTileBytes in dynamic shared memory.
+constexpr uint32_t kTmaTileBytes = 32768;
+constexpr int kTmaStages = 6;
+constexpr uint32_t kVecTileBytes = 32768;
+constexpr int kVecThreads = 512;
+
+/// Per-device runtime facts the launchers need (SM count, the status word).
+struct DeviceCtx {
+    int device = -1;
+    int sms = 0;
+    uint32_t* status = nullptr;
+};
+/// Returns the context of the CURRENT device, creating it on first use.  Null on failure (error set).
+DeviceCtx* current_ctx();
+
+/// Thread-local error message used by skv_last_error().
+void set_error(const std::string& message);
+int fail(int code, const std::string& message);
+int cuda_fail(cudaError_t e, const char* what);
+
+/// Launch one copy kernel for a prepared plan.  `engine` is SKV_COPY_TMA or SKV_COPY_VEC.
+int launch_copy(const CopyPlan& plan, uint64_t total_tiles, int engine, const DeviceCtx& ctx, cudaStream_t stream);
+/// Enqueue the flag kernels.
+int launch_signal(uint64_t* flag, uint64_t value, cudaStream_t stream);
+int launch_wait(const uint64_t* flag, uint64_t value, uint64_t timeout_ns, uint32_t* status, cudaStream_t stream);
+
+}  // namespace skv
