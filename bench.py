@@ -25,7 +25,6 @@ import argparse
 import ctypes
 import json
 import os
-import subprocess
 import sys
 import threading
 import time
@@ -48,12 +47,13 @@ PROFILE_TRAFFIC = os.path.join(ROOT, "profiles", "traffic.json")
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
-    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--tokens", type=int, default=32768)
     ap.add_argument("--engine", default="tma", choices=["tma", "vec"])
     ap.add_argument("--seed", type=int, default=1)
+    ap.add_argument("--pool-blocks", type=int, default=4096, help="slots per pool (the configs use 4,096)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     return ap.parse_args()
@@ -76,48 +76,63 @@ def traffic_for(kernel: str, workload: str):
 
 
 class Clocks:
-    """nvidia-smi samples during the timed region."""
+    """SM clock and clock-event reasons sampled DURING the timed region: NVML polled from a thread every
+    ~1 ms (a 32K handoff step is ~0.3 ms, far below nvidia-smi's sampling interval)."""
 
-    def __init__(self, index: int):
-        self.index = index
-        self.proc = None
+    REASONS = {"hw_slowdown": 0x8, "hw_thermal_slowdown": 0x40, "sw_thermal_slowdown": 0x20, "sw_power_cap": 0x4,
+               "hw_power_brake_slowdown": 0x80}
+
+    def __init__(self, cuda_index: int):
+        self.cuda_index = cuda_index
+        self.samples = []
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._thread = None
+
+    def _handle(self, nv):
+        import torch
+        p = torch.cuda.get_device_properties(self.cuda_index)
+        bus = f"{p.pci_domain_id:08x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0"
+        try:
+            return nv.nvmlDeviceGetHandleByPciBusId(bus)
+        except Exception:
+            return nv.nvmlDeviceGetHandleByIndex(self.cuda_index)
 
     def __enter__(self):
-        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
-             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
-             "clocks_event_reasons.sw_power_cap")
         try:
-            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={q}",
-                                          "--format=csv,noheader,nounits", "-lms", "100"],
-                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            import pynvml as nv
+            nv.nvmlInit()
+            h = self._handle(nv)
+            self.max_mhz = float(nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM))
         except Exception:
-            self.proc = None
+            return self
+
+        def poll():
+            while not self._stop.is_set():
+                try:
+                    self.samples.append((float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)),
+                                         int(nv.nvmlDeviceGetCurrentClocksEventReasons(h))))
+                except Exception:
+                    pass
+                time.sleep(0.001)
+
+        self._thread = threading.Thread(target=poll, daemon=True)
+        self._thread.start()
+        time.sleep(0.003)
         return self
 
     def __exit__(self, *a):
-        self.rows = []
-        if self.proc is None:
-            return
-        self.proc.terminate()
-        try:
-            out, _ = self.proc.communicate(timeout=5)
-        except Exception:
-            self.proc.kill()
-            out = ""
-        for line in out.splitlines():
-            parts = [p.strip() for p in line.split(",")]
-            if len(parts) >= 8:
-                self.rows.append(parts)
+        self._stop.set()
+        if self._thread is not None:
+            self._thread.join(timeout=2)
 
     def summary(self) -> dict:
-        if not getattr(self, "rows", None):
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
-        sm = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
-        mx = [float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit()]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in self.rows for i in range(4) if r[4 + i] == "Active"})
-        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": reasons, "samples": len(self.rows)}
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["unsampled"], "samples": 0}
+        sm = [c for c, _ in self.samples]
+        reasons = sorted({n for _, bits in self.samples for n, b in self.REASONS.items() if bits & b})
+        return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": self.max_mhz, "reasons": reasons,
+                "samples": len(self.samples), "source": "NVML, 1 ms polling during the timed region"}
 
 
 # ------------------------------------------------------------------------------------------------ workloads
@@ -305,8 +320,9 @@ def run_single(args, torch) -> None:
     t = args.tokens
     engine = skv.COPY_TMA if args.engine == "tma" else skv.COPY_VEC
     torch.cuda.set_device(0)
-    src = SeqOnGpu(torch, kg, t, 4096, seed=args.seed, fill=True)
-    dst = SeqOnGpu(torch, kg, t, 4096, seed=args.seed + 1000, fill=False)
+    n_blocks = max(args.pool_blocks, kg.n_qsa * kg.blocks(t))
+    src = SeqOnGpu(torch, kg, t, n_blocks, seed=args.seed, fill=True)
+    dst = SeqOnGpu(torch, kg, t, n_blocks, seed=args.seed + 1000, fill=False)
     segs = skv.kv_segments_pool_to_pool(src.ps, dst.ps) + skv.state_segments(src.ps, dst.gdn, dst.ids)
     arr = (skv.Segment * len(segs))(*segs)
     stream = torch.cuda.current_stream()
