@@ -120,6 +120,27 @@ typedef struct skv_segment {
  * device, peer (P2P over NVLink) or mapped pinned host memory.  n_segs <= SKV_COPY_MAX_SEGMENTS. */
 SKV_API int skv_copy(const skv_segment* segs, int n_segs, int engine, void* stream);
 
+/* skv_copy_noalloc - the same copy for callers that cannot allocate device memory.
+ * No counterpart in the reference (its park path only has synchronous cudaMemcpy calls).
+ *
+ * Who needs it: an engine whose token path must not allocate (the reference's session requires zero
+ * token-path allocations, and a park or mount happens between tokens of a running server), a caller
+ * that has given every free byte of HBM to its block pool, and any caller that cannot afford the implicit
+ * device-wide synchronisation a first cudaMalloc can cause while other streams are decoding.  skv_copy
+ * allocates a small status word on a device's first use; this entry point allocates nothing, ever.
+ *
+ * It moves the segments with the vector engine in one copy launch, up to SKV_NOALLOC_MAX_SEGMENTS
+ * segments per call (skv_copy takes 64).  Its plan and status word live in one fixed-size device array
+ * of the library (about 41 KB per GPU, held until the process exits).  More segments than the maximum
+ * is refused with SKV_ERANGE before anything is enqueued.
+ *   status_out  optional; receives the call's SKV_STATUS_* bits (device or mapped pinned host memory),
+ *               written in stream order after the copy.
+ * Calls share the array: calls issued on one stream are ordered and safe, calls that overlap on the GPU
+ * (other streams of the same device) race on it.  The first call on a device does a one-time set-up
+ * (symbol address, SM count); make it before any stream capture. */
+#define SKV_NOALLOC_MAX_SEGMENTS 512
+SKV_API int skv_copy_noalloc(const skv_segment* segs, int n_segs, uint32_t* status_out, void* stream);
+
 /* The device status word of `device` (OR of SKV_STATUS_* since the last clear); synchronises `stream`. */
 SKV_API int skv_query_status(int device, void* stream, uint32_t* out_status);
 SKV_API int skv_clear_status(int device, void* stream);

@@ -22,7 +22,10 @@
 // returns.  No trap, no assert, no unbounded spin.
 #include "skv_internal.h"
 
+#include <algorithm>
 #include <cstdio>
+#include <mutex>
+#include <string>
 
 namespace skv {
 namespace {
@@ -219,7 +222,8 @@ __global__ void __launch_bounds__(32, 1) copy_tma_kernel(const __grid_constant__
     for (; k < mine; ++k) {
         const int st = (int) (k % kTmaStages);
         const uint32_t phase = (uint32_t) ((k / kTmaStages) & 1u);
-        if (!mbar_wait_bounded(&bars[st], phase)) {
+        // warp-uniform verdict: every lane leaves the loop together, so no later collective splits the warp
+        if (!__all_sync(0xffffffffu, mbar_wait_bounded(&bars[st], phase))) {
             timed_out = true;
             break;
         }
@@ -367,3 +371,246 @@ int launch_wait(const uint64_t* flag, uint64_t value, uint64_t timeout_ns, uint3
 }
 
 }  // namespace skv
+
+// ================================================================ allocation-free entry point
+//
+// skv_copy_noalloc: the vector copy engine for callers that must not allocate device memory.  The engine
+// that skv_copy launches needs scratch beyond its inputs and outputs (its status word, which skv_copy
+// cudaMallocs once per device), and its plan is capped at SKV_COPY_MAX_SEGMENTS by the kernel-parameter
+// size.  Here both live in ONE file-scope device array of fixed size: the plan (up to
+// SKV_NOALLOC_MAX_SEGMENTS segments) and the status word.  A small writer kernel fills the array in stream
+// order from descriptors passed as kernel parameters, then the copy kernel reads it.
+//
+// Every call shares the array (one instance per device) and it keeps the last call's contents.  Calls
+// issued on ONE stream are ordered and safe; calls that overlap on the GPU (different streams of the same
+// device, or host threads racing on one stream) race on the plan and the status word.  The first call on a
+// device performs the set-up (cudaGetSymbolAddress, the SM count); make that first call before any stream
+// capture.
+namespace skv {
+namespace {
+
+struct NoallocPlan {
+    uint32_t status;       // SKV_STATUS_* bits of the current call; cleared by the writer of the first chunk
+    uint32_t n_segs;
+    uint64_t reserved;
+    uint64_t tile_end[SKV_NOALLOC_MAX_SEGMENTS];
+    SegDev seg[SKV_NOALLOC_MAX_SEGMENTS];
+};
+constexpr size_t kNoallocScratchBytes = (sizeof(NoallocPlan) + 255) / 256 * 256;
+
+/// The scratch: a fixed-size array every GPU that loads the library holds until the process exits.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoallocScratchBytes];
+
+constexpr int kNoallocChunk = 128;   // descriptors per writer launch (about 10 KB of kernel parameters)
+
+struct NoallocChunk {
+    uint32_t first;        // index of chunk[0] in the plan
+    uint32_t count;
+    uint32_t n_segs;       // the whole plan's segment count
+    uint32_t clear_status; // 1 on the first chunk of a call
+    uint64_t tile_end[kNoallocChunk];
+    SegDev seg[kNoallocChunk];
+};
+
+__global__ void noalloc_plan_writer(const __grid_constant__ NoallocChunk c, NoallocPlan* plan) {
+    const uint32_t i = threadIdx.x;
+    if (i < c.count) {
+        plan->seg[c.first + i] = c.seg[i];
+        plan->tile_end[c.first + i] = c.tile_end[i];
+    }
+    if (i == 0) {
+        plan->n_segs = c.n_segs;
+        if (c.clear_status) plan->status = 0;
+    }
+}
+
+__device__ __forceinline__ int noalloc_locate(const NoallocPlan* plan, uint64_t t) {
+    int lo = 0, hi = (int) plan->n_segs - 1;
+    while (lo < hi) {
+        const int mid = (lo + hi) >> 1;
+        if (t < plan->tile_end[mid]) hi = mid;
+        else lo = mid + 1;
+    }
+    return lo;
+}
+
+/// The vector engine (same addressing, checks and status bits as copy_vec_kernel) over the scratch plan.
+__global__ void __launch_bounds__(kVecThreads) copy_vec_noalloc_kernel(const NoallocPlan* plan, uint64_t total_tiles) {
+    __shared__ int64_t s_src[kVecMaxPages];
+    __shared__ int64_t s_dst[kVecMaxPages];
+    uint32_t* status = const_cast<uint32_t*>(&plan->status);
+    for (uint64_t t = blockIdx.x; t < total_tiles; t += gridDim.x) {
+        const int s = noalloc_locate(plan, t);
+        const SegDev sg = plan->seg[s];
+        const uint64_t local = t - (s ? plan->tile_end[s - 1] : 0);
+        if (sg.page_bytes == 0) {
+            const uint64_t off = local * sg.tile_bytes;
+            const uint32_t n16 = (uint32_t) (min(sg.tile_bytes, sg.bytes - off) >> 4);
+            for (uint32_t i = threadIdx.x; i < n16; i += kVecThreads * kVecUnroll) {
+                uint4 v[kVecUnroll];
+#pragma unroll
+                for (int u = 0; u < kVecUnroll; ++u) {
+                    const uint32_t e = i + (uint32_t) u * kVecThreads;
+                    if (e < n16) v[u] = ld_stream(sg.src + off + (uint64_t) e * 16);
+                }
+#pragma unroll
+                for (int u = 0; u < kVecUnroll; ++u) {
+                    const uint32_t e = i + (uint32_t) u * kVecThreads;
+                    if (e < n16) st_plain(sg.dst + off + (uint64_t) e * 16, v[u]);
+                }
+            }
+            continue;
+        }
+        const uint32_t pb = sg.page_bytes;
+        const uint64_t page0 = local * sg.pages_per_tile;
+        const uint32_t np = (uint32_t) min((uint64_t) sg.pages_per_tile, sg.bytes / pb - page0);
+        __syncthreads();
+        for (uint32_t p = threadIdx.x; p < np; p += kVecThreads) {
+            const LanePage lp = lane_page(sg, page0 + p, true, status);
+            s_src[p] = lp.good ? lp.s : -1;
+            s_dst[p] = lp.good ? lp.d : -1;
+        }
+        __syncthreads();
+        const uint32_t per_page16 = pb >> 4;
+        const uint32_t n16 = np * per_page16;
+        for (uint32_t i = threadIdx.x; i < n16; i += kVecThreads * kVecUnroll) {
+            uint4 v[kVecUnroll];
+            int64_t da[kVecUnroll];
+#pragma unroll
+            for (int u = 0; u < kVecUnroll; ++u) {
+                const uint32_t e = i + (uint32_t) u * kVecThreads;
+                da[u] = -1;
+                if (e < n16) {
+                    const uint32_t p = e / per_page16, w = e - p * per_page16;
+                    const int64_t src_page = s_src[p];
+                    if (src_page >= 0) {
+                        v[u] = ld_stream(sg.src + (uint64_t) src_page * pb + (uint64_t) w * 16);
+                        da[u] = s_dst[p] * (int64_t) pb + (int64_t) w * 16;
+                    }
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < kVecUnroll; ++u)
+                if (da[u] >= 0) st_plain(sg.dst + da[u], v[u]);
+        }
+    }
+}
+
+constexpr int kNoallocMaxDevices = 64;
+std::mutex g_noalloc_mu;
+NoallocPlan* g_noalloc_ptr[kNoallocMaxDevices] = {};
+int g_noalloc_sms[kNoallocMaxDevices] = {};
+
+/// Per-device set-up, once, with that device current: the scratch's device address and the SM count.
+int noalloc_setup(int dev, NoallocPlan** plan, int* sms) {
+    if (dev < 0 || dev >= kNoallocMaxDevices) return fail(SKV_EINVAL, "skv_copy_noalloc: device ordinal out of range");
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (!g_noalloc_ptr[dev]) {
+        void* p = nullptr;
+        cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess) return cuda_fail(e, "skv_copy_noalloc: cudaGetSymbolAddress");
+        int n = 0;
+        e = cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+        if (e != cudaSuccess) return cuda_fail(e, "skv_copy_noalloc: cudaDeviceGetAttribute");
+        g_noalloc_sms[dev] = n;
+        g_noalloc_ptr[dev] = static_cast<NoallocPlan*>(p);
+    }
+    *plan = g_noalloc_ptr[dev];
+    *sms = g_noalloc_sms[dev];
+    return SKV_OK;
+}
+
+}  // namespace
+}  // namespace skv
+
+extern "C" int skv_copy_noalloc(const skv_segment* segs, int n_segs, uint32_t* status_out, void* stream_ptr) {
+    using namespace skv;
+    if (n_segs < 0 || (n_segs && !segs)) return fail(SKV_EINVAL, "skv_copy_noalloc: bad segment list");
+    if (n_segs > SKV_NOALLOC_MAX_SEGMENTS)
+        return fail(SKV_ERANGE, "skv_copy_noalloc: " + std::to_string(n_segs) + " segments exceed the static plan's " +
+                                    std::to_string(SKV_NOALLOC_MAX_SEGMENTS) + "-segment maximum");
+    int dev = -1;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_fail(e, "skv_copy_noalloc: cudaGetDevice");
+    NoallocPlan* plan = nullptr;
+    int sms = 0;
+    if (const int rc = noalloc_setup(dev, &plan, &sms)) return rc;
+    const cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+
+    // validate everything before enqueuing anything (the same rules as the vector engine of skv_copy)
+    NoallocChunk chunk;
+    uint64_t total_tiles = 0;
+    uint32_t kept = 0;
+    int launched_chunks = 0;
+    auto flush = [&](bool last) -> int {
+        if (chunk.count == 0 && !(last && launched_chunks == 0)) return SKV_OK;
+        chunk.clear_status = launched_chunks == 0 ? 1u : 0u;
+        noalloc_plan_writer<<<1, kNoallocChunk, 0, stream>>>(chunk, plan);
+        const cudaError_t le = cudaGetLastError();
+        if (le != cudaSuccess) return cuda_fail(le, "skv_copy_noalloc: plan writer launch");
+        ++launched_chunks;
+        chunk.first += chunk.count;
+        chunk.count = 0;
+        return SKV_OK;
+    };
+    // first pass: validation only
+    for (int i = 0; i < n_segs; ++i) {
+        const skv_segment& s = segs[i];
+        if (s.bytes == 0) continue;
+        const std::string where = "skv_copy_noalloc: segment " + std::to_string(i) + ": ";
+        if (!s.src || !s.dst) return fail(SKV_EINVAL, where + "missing buffer");
+        if ((reinterpret_cast<uintptr_t>(s.src) & 15u) || (reinterpret_cast<uintptr_t>(s.dst) & 15u) || s.bytes % 16)
+            return fail(SKV_EINVAL, where + "buffers must be 16-byte aligned and bytes a multiple of 16");
+        if (s.src_pages || s.dst_pages) {
+            if (s.page_bytes == 0 || s.page_bytes % 16 || s.bytes % s.page_bytes)
+                return fail(SKV_EINVAL, where + "a paged side needs page_bytes a multiple of 16 dividing bytes");
+            if ((s.src_pages && s.src_page_limit <= 0) || (s.dst_pages && s.dst_page_limit <= 0))
+                return fail(SKV_EINVAL, where + "a paged side needs a positive page limit");
+        }
+    }
+    // second pass: the plan, written into the scratch by the writer kernel in chunks
+    chunk.first = 0;
+    chunk.count = 0;
+    for (int i = 0; i < n_segs; ++i) {
+        const skv_segment& s = segs[i];
+        if (s.bytes == 0) continue;
+        ++kept;
+    }
+    chunk.n_segs = kept;
+    for (int i = 0; i < n_segs; ++i) {
+        const skv_segment& s = segs[i];
+        if (s.bytes == 0) continue;
+        SegDev d{};
+        d.src = static_cast<const uint8_t*>(s.src);
+        d.dst = static_cast<uint8_t*>(s.dst);
+        d.src_pages = s.src_pages;
+        d.dst_pages = s.dst_pages;
+        d.bytes = s.bytes;
+        d.src_page_limit = s.src_page_limit;
+        d.dst_page_limit = s.dst_page_limit;
+        if (s.src_pages || s.dst_pages) {
+            d.page_bytes = s.page_bytes;
+            d.pages_per_tile = std::max<uint32_t>(1u, std::min<uint32_t>(512u, kVecTileBytes / s.page_bytes));
+            d.tile_bytes = (uint64_t) d.pages_per_tile * s.page_bytes;
+        } else {
+            d.tile_bytes = kVecTileBytes;
+        }
+        total_tiles += (d.bytes + d.tile_bytes - 1) / d.tile_bytes;
+        chunk.seg[chunk.count] = d;
+        chunk.tile_end[chunk.count] = total_tiles;
+        if (++chunk.count == (uint32_t) kNoallocChunk)
+            if (const int rc = flush(false)) return rc;
+    }
+    if (const int rc = flush(true)) return rc;   // also clears the status word when every segment was empty
+    if (total_tiles) {
+        const unsigned grid = (unsigned) std::min<uint64_t>(total_tiles, (uint64_t) sms * 4);
+        copy_vec_noalloc_kernel<<<grid, kVecThreads, 0, stream>>>(plan, total_tiles);
+        const cudaError_t le = cudaGetLastError();
+        if (le != cudaSuccess) return cuda_fail(le, "skv_copy_noalloc: copy kernel launch");
+    }
+    if (status_out) {
+        e = cudaMemcpyAsync(status_out, &plan->status, sizeof(uint32_t), cudaMemcpyDefault, stream);
+        if (e != cudaSuccess) return cuda_fail(e, "skv_copy_noalloc: status copy");
+    }
+    return SKV_OK;
+}

@@ -28,6 +28,7 @@ STATUS_BAD_SRC_PAGE, STATUS_BAD_DST_PAGE, STATUS_WAIT_TIMEOUT = 0x1, 0x2, 0x4
 COPY_AUTO, COPY_TMA, COPY_VEC = 0, 1, 2
 PARK_DIRECT, PARK_STAGED = 1, 2
 MAX_SEGMENTS = 64
+NOALLOC_MAX_SEGMENTS = 512
 
 PAGE_CELLS = 4
 BLOCK_TOKENS = 256
@@ -63,6 +64,7 @@ _SIGNATURES = {
     "skv_pool_scramble": ([C.c_void_p, C.c_uint64], C.c_int),
     "skv_expand_block_table": ([C.c_void_p, C.c_int64, C.c_int64, C.c_int64, C.c_int64, C.c_void_p], C.c_int),
     "skv_copy": ([C.c_void_p, C.c_int, C.c_int, C.c_void_p], C.c_int),
+    "skv_copy_noalloc": ([C.c_void_p, C.c_int, C.c_void_p, C.c_void_p], C.c_int),
     "skv_query_status": ([C.c_int, C.c_void_p, C.POINTER(C.c_uint32)], C.c_int),
     "skv_clear_status": ([C.c_int, C.c_void_p], C.c_int),
     "skv_host_alloc": ([C.c_uint64, C.POINTER(C.c_void_p)], C.c_int),
