@@ -141,6 +141,12 @@ SKV_API int skv_copy(const skv_segment* segs, int n_segs, int engine, void* stre
 #define SKV_NOALLOC_MAX_SEGMENTS 512
 SKV_API int skv_copy_noalloc(const skv_segment* segs, int n_segs, uint32_t* status_out, void* stream);
 
+/* Copy-engine geometry, process-wide.  The TMA engine runs tma_ctas_per_sm CTAs per SM, each with a ring of
+ * tma_stages x tma_tile_bytes of shared memory (the rings must fit the SM's 228 KB together); the vector
+ * engine runs vec_ctas_per_sm CTAs of 512 threads per SM.  Defaults are the values measured best on B200. */
+SKV_API int skv_set_copy_tuning(int tma_stages, uint32_t tma_tile_bytes, int tma_ctas_per_sm, int vec_ctas_per_sm);
+SKV_API int skv_get_copy_tuning(int* tma_stages, uint32_t* tma_tile_bytes, int* tma_ctas_per_sm, int* vec_ctas_per_sm);
+
 /* The device status word of `device` (OR of SKV_STATUS_* since the last clear); synchronises `stream`. */
 SKV_API int skv_query_status(int device, void* stream, uint32_t* out_status);
 SKV_API int skv_clear_status(int device, void* stream);

@@ -17,6 +17,8 @@ namespace skv {
 
 namespace {
 thread_local std::string t_error;
+std::mutex g_tuning_mu;
+Tuning g_tuning;
 std::mutex g_ctx_mu;
 std::vector<std::unique_ptr<DeviceCtx>> g_ctx;   // indexed by device ordinal
 
@@ -31,6 +33,11 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 }  // namespace
 
 void set_error(const std::string& message) { t_error = message; }
+
+Tuning tuning() {
+    std::lock_guard<std::mutex> lock(g_tuning_mu);
+    return g_tuning;
+}
 
 int fail(int code, const std::string& message) {
     t_error = message;
@@ -72,10 +79,13 @@ DeviceCtx* current_ctx() {
 
 /// Validate the public segments and turn them into a kernel plan.  Zero-byte segments are dropped.
 static int build_plan(const skv_segment* segs, int n_segs, int engine, CopyPlan& plan, uint64_t& total_tiles) {
+    const Tuning tu = tuning();
     if (n_segs < 0 || n_segs > SKV_COPY_MAX_SEGMENTS || (n_segs && !segs))
         return fail(SKV_EINVAL, "skv_copy: segment count must be in [0, SKV_COPY_MAX_SEGMENTS]");
     if (engine != SKV_COPY_TMA && engine != SKV_COPY_VEC) return fail(SKV_EINVAL, "skv_copy: unknown copy engine");
     std::memset(&plan, 0, sizeof plan);
+    plan.tma_stages = tu.tma_stages;
+    plan.tma_tile = tu.tma_tile;
     total_tiles = 0;
     int k = 0;
     for (int i = 0; i < n_segs; ++i) {
@@ -102,15 +112,15 @@ static int build_plan(const skv_segment* segs, int n_segs, int engine, CopyPlan&
                 return fail(SKV_EINVAL, std::string(where) + "a paged side needs a positive page limit");
             d.page_bytes = s.page_bytes;
             if (engine == SKV_COPY_TMA) {
-                if (s.page_bytes < 1024 || s.page_bytes > kTmaTileBytes)
-                    return fail(SKV_EINVAL, std::string(where) + "the TMA engine stages pages of 1 KiB to 32 KiB");
-                d.pages_per_tile = std::min<uint32_t>(32u, kTmaTileBytes / s.page_bytes);
+                if (s.page_bytes < 1024 || s.page_bytes > tu.tma_tile)
+                    return fail(SKV_EINVAL, std::string(where) + "the TMA engine stages pages of 1 KiB up to its tile size");
+                d.pages_per_tile = std::min<uint32_t>(32u, tu.tma_tile / s.page_bytes);
             } else {
                 d.pages_per_tile = std::max<uint32_t>(1u, std::min<uint32_t>(512u, kVecTileBytes / s.page_bytes));
             }
             d.tile_bytes = (uint64_t) d.pages_per_tile * s.page_bytes;
         } else {
-            d.tile_bytes = engine == SKV_COPY_TMA ? kTmaTileBytes : kVecTileBytes;
+            d.tile_bytes = engine == SKV_COPY_TMA ? tu.tma_tile : kVecTileBytes;
         }
         total_tiles += (d.bytes + d.tile_bytes - 1) / d.tile_bytes;
         plan.seg[k] = d;
@@ -123,10 +133,11 @@ static int build_plan(const skv_segment* segs, int n_segs, int engine, CopyPlan&
 
 /// AUTO: the bulk engine when every buffer is this device's own memory and every page granule suits it.
 static int pick_engine(const skv_segment* segs, int n_segs, int device) {
+    const uint32_t tile = tuning().tma_tile;
     for (int i = 0; i < n_segs; ++i) {
         const skv_segment& s = segs[i];
         if (s.bytes == 0) continue;
-        if ((s.src_pages || s.dst_pages) && (s.page_bytes < 1024 || s.page_bytes > kTmaTileBytes)) return SKV_COPY_VEC;
+        if ((s.src_pages || s.dst_pages) && (s.page_bytes < 1024 || s.page_bytes > tile)) return SKV_COPY_VEC;
         for (const void* p : {s.src, static_cast<const void*>(s.dst)}) {
             cudaPointerAttributes a{};
             if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
@@ -301,6 +312,32 @@ int skv_copy(const skv_segment* segs, int n_segs, int engine, void* stream) {
     if (const int rc = build_plan(segs, n_segs, engine, plan, tiles)) return rc;
     plan.status = ctx->status;
     return launch_copy(plan, tiles, engine, *ctx, static_cast<cudaStream_t>(stream));
+}
+
+int skv_set_copy_tuning(int tma_stages, uint32_t tma_tile_bytes, int tma_ctas_per_sm, int vec_ctas_per_sm) {
+    if (tma_stages < 2 || tma_stages > kTmaMaxStages || tma_tile_bytes < kTmaMinTileBytes ||
+        tma_tile_bytes > kTmaMaxTileBytes || tma_tile_bytes % 1024 || tma_ctas_per_sm < 1 || tma_ctas_per_sm > 8 ||
+        vec_ctas_per_sm < 1 || vec_ctas_per_sm > 8)
+        return fail(SKV_EINVAL, "skv_set_copy_tuning: stages in [2, 12], tile a multiple of 1 KiB in [4, 64] KiB, "
+                                "CTAs per SM in [1, 8]");
+    const size_t per_cta = tma_smem_bytes(tma_stages, tma_tile_bytes) + 1024;   // + the per-CTA reservation
+    if (per_cta > 227 * 1024 || per_cta * (size_t) tma_ctas_per_sm > kSmemPerSm)
+        return fail(SKV_ERANGE, "skv_set_copy_tuning: the TMA rings do not fit the SM's shared memory");
+    std::lock_guard<std::mutex> lock(g_tuning_mu);
+    g_tuning.tma_stages = tma_stages;
+    g_tuning.tma_tile = tma_tile_bytes;
+    g_tuning.tma_ctas_per_sm = tma_ctas_per_sm;
+    g_tuning.vec_ctas_per_sm = vec_ctas_per_sm;
+    return SKV_OK;
+}
+
+int skv_get_copy_tuning(int* tma_stages, uint32_t* tma_tile_bytes, int* tma_ctas_per_sm, int* vec_ctas_per_sm) {
+    const Tuning t = tuning();
+    if (tma_stages) *tma_stages = t.tma_stages;
+    if (tma_tile_bytes) *tma_tile_bytes = t.tma_tile;
+    if (tma_ctas_per_sm) *tma_ctas_per_sm = t.tma_ctas_per_sm;
+    if (vec_ctas_per_sm) *vec_ctas_per_sm = t.vec_ctas_per_sm;
+    return SKV_OK;
 }
 
 int skv_query_status(int device, void* stream, uint32_t* out_status) {

@@ -2,12 +2,13 @@
 //
 // Every byte the path moves goes through ONE of two copy engines, driven by the same segment/tile plan:
 //
-//   copy_tma_kernel  a ring of kTmaStages shared-memory tiles per CTA (one CTA per SM).  One warp issues
+//   copy_tma_kernel  a ring of shared-memory tiles per CTA (geometry in the plan; by default 3 CTAs per SM,
+//                    each 4 stages x 16 KiB, so three issuing warps per SM overlap their table loads).  One warp issues
 //                    cp.async.bulk global->shared loads tracked by an mbarrier per stage, then
 //                    cp.async.bulk shared->global stores tracked by bulk groups.  Table lookups are done
 //                    32 pages at a time by the warp's lanes, and consecutive pages (the 64 pages of one
 //                    256-token block are consecutive in a pool slot) merge into ONE bulk operation, so a
-//                    32 KiB tile of K is one load and one store however the block table is permuted.
+//                    tile of K is one load and one store however the block table is permuted.
 //   copy_vec_kernel  16-byte vector loads (non-coherent, no L1 allocation) and stores, 4 in flight per
 //                    thread, for destinations the bulk engine is not used on: peer memory (the P2P push
 //                    over NVLink) and mapped pinned host memory (the direct park), and for page granules
@@ -198,30 +199,32 @@ __device__ __forceinline__ void tma_issue_load(const CopyPlan& plan, uint64_t t,
     stash.smem_off[lane] = (uint32_t) lane * (uint32_t) pb;
 }
 
-__global__ void __launch_bounds__(32, 1) copy_tma_kernel(const __grid_constant__ CopyPlan plan, uint64_t total_tiles) {
+__global__ void __launch_bounds__(32) copy_tma_kernel(const __grid_constant__ CopyPlan plan, uint64_t total_tiles) {
     extern __shared__ __align__(1024) uint8_t smem[];
+    const int stages = plan.tma_stages;
+    const uint32_t tile = plan.tma_tile;
     uint8_t* ring = smem;
-    StageStash* stash = reinterpret_cast<StageStash*>(smem + (size_t) kTmaStages * kTmaTileBytes);
-    uint64_t* bars = reinterpret_cast<uint64_t*>(stash + kTmaStages);
+    StageStash* stash = reinterpret_cast<StageStash*>(smem + (size_t) stages * tile);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(stash + stages);
     const int lane = (int) threadIdx.x;
 
     if (lane == 0)
-        for (int s = 0; s < kTmaStages; ++s) mbar_init(&bars[s], 1);
+        for (int s = 0; s < stages; ++s) mbar_init(&bars[s], 1);
     fence_proxy_async_smem();
     __syncwarp();
 
     const uint64_t first = blockIdx.x, step = gridDim.x;
     const uint64_t mine = first < total_tiles ? (total_tiles - first + step - 1) / step : 0;
     uint64_t issued = 0;
-    for (; issued < mine && issued < (uint64_t) kTmaStages; ++issued)
-        tma_issue_load(plan, first + issued * step, ring + (issued % kTmaStages) * kTmaTileBytes,
-                       &bars[issued % kTmaStages], stash[issued % kTmaStages], lane);
+    for (; issued < mine && issued < (uint64_t) stages; ++issued)
+        tma_issue_load(plan, first + issued * step, ring + (issued % stages) * tile, &bars[issued % stages],
+                       stash[issued % stages], lane);
 
     uint64_t k = 0;
     bool timed_out = false;
     for (; k < mine; ++k) {
-        const int st = (int) (k % kTmaStages);
-        const uint32_t phase = (uint32_t) ((k / kTmaStages) & 1u);
+        const int st = (int) (k % stages);
+        const uint32_t phase = (uint32_t) ((k / stages) & 1u);
         // warp-uniform verdict: every lane leaves the loop together, so no later collective splits the warp
         if (!__all_sync(0xffffffffu, mbar_wait_bounded(&bars[st], phase))) {
             timed_out = true;
@@ -229,14 +232,14 @@ __global__ void __launch_bounds__(32, 1) copy_tma_kernel(const __grid_constant__
         }
         fence_proxy_async_smem();
         const uint32_t len = stash[st].store_len[lane];
-        if (len) bulk_store(stash[st].store_addr[lane], ring + (size_t) st * kTmaTileBytes + stash[st].smem_off[lane], len);
+        if (len) bulk_store(stash[st].store_addr[lane], ring + (size_t) st * tile + stash[st].smem_off[lane], len);
         bulk_commit();
         // refill the stage of tile k-1 once its store has finished reading shared memory
         if (k >= 1 && issued < mine) {
             bulk_wait_read_1();
             __syncwarp();
-            const int rs = (int) ((k - 1) % kTmaStages);
-            tma_issue_load(plan, first + issued * step, ring + (size_t) rs * kTmaTileBytes, &bars[rs], stash[rs], lane);
+            const int rs = (int) ((k - 1) % stages);
+            tma_issue_load(plan, first + issued * step, ring + (size_t) rs * tile, &bars[rs], stash[rs], lane);
             ++issued;
         }
     }
@@ -244,7 +247,7 @@ __global__ void __launch_bounds__(32, 1) copy_tma_kernel(const __grid_constant__
         if (lane == 0) atomicOr(plan.status, SKV_STATUS_WAIT_TIMEOUT);
         // drain the loads still in flight into this CTA's shared memory, each wait bounded again
         for (uint64_t j = k; j < issued; ++j)
-            (void) mbar_wait_bounded(&bars[j % kTmaStages], (uint32_t) ((j / kTmaStages) & 1u));
+            (void) mbar_wait_bounded(&bars[j % stages], (uint32_t) ((j / stages) & 1u));
     }
     bulk_wait_all();
 }
@@ -338,20 +341,24 @@ __global__ void wait_kernel(const uint64_t* flag, uint64_t value, uint64_t timeo
 
 }  // namespace
 
-int launch_copy(const CopyPlan& plan, uint64_t total_tiles, int engine, const DeviceCtx& ctx, cudaStream_t stream) {
+size_t tma_smem_bytes(int stages, uint32_t tile) {
+    return (size_t) stages * tile + sizeof(StageStash) * (size_t) stages + 8 * (size_t) stages;
+}
+
+int launch_copy(const CopyPlan& plan, uint64_t total_tiles, int engine, DeviceCtx& ctx, cudaStream_t stream) {
     if (total_tiles == 0) return SKV_OK;
+    const Tuning tu = tuning();
     if (engine == SKV_COPY_TMA) {
-        const size_t smem = (size_t) kTmaStages * kTmaTileBytes + sizeof(StageStash) * kTmaStages + 8 * kTmaStages;
-        static thread_local int configured_device = -1;
-        if (configured_device != ctx.device) {
+        const size_t smem = tma_smem_bytes(plan.tma_stages, plan.tma_tile);
+        if (ctx.tma_smem_configured < smem) {
             const cudaError_t e = cudaFuncSetAttribute(copy_tma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem);
             if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(copy_tma_kernel)");
-            configured_device = ctx.device;
+            ctx.tma_smem_configured = smem;
         }
-        const unsigned grid = (unsigned) std::min<uint64_t>(total_tiles, (uint64_t) ctx.sms);
+        const unsigned grid = (unsigned) std::min<uint64_t>(total_tiles, (uint64_t) ctx.sms * tu.tma_ctas_per_sm);
         copy_tma_kernel<<<grid, 32, smem, stream>>>(plan, total_tiles);
     } else {
-        const unsigned grid = (unsigned) std::min<uint64_t>(total_tiles, (uint64_t) ctx.sms * 4);
+        const unsigned grid = (unsigned) std::min<uint64_t>(total_tiles, (uint64_t) ctx.sms * tu.vec_ctas_per_sm);
         copy_vec_kernel<<<grid, kVecThreads, 0, stream>>>(plan, total_tiles);
     }
     const cudaError_t e = cudaGetLastError();
@@ -538,7 +545,7 @@ extern "C" int skv_copy_noalloc(const skv_segment* segs, int n_segs, uint32_t* s
     const cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
 
     // validate everything before enqueuing anything (the same rules as the vector engine of skv_copy)
-    NoallocChunk chunk;
+    NoallocChunk chunk{};
     uint64_t total_tiles = 0;
     uint32_t kept = 0;
     int launched_chunks = 0;

@@ -65,6 +65,8 @@ _SIGNATURES = {
     "skv_expand_block_table": ([C.c_void_p, C.c_int64, C.c_int64, C.c_int64, C.c_int64, C.c_void_p], C.c_int),
     "skv_copy": ([C.c_void_p, C.c_int, C.c_int, C.c_void_p], C.c_int),
     "skv_copy_noalloc": ([C.c_void_p, C.c_int, C.c_void_p, C.c_void_p], C.c_int),
+    "skv_set_copy_tuning": ([C.c_int, C.c_uint32, C.c_int, C.c_int], C.c_int),
+    "skv_get_copy_tuning": ([C.POINTER(C.c_int), C.POINTER(C.c_uint32), C.POINTER(C.c_int), C.POINTER(C.c_int)], C.c_int),
     "skv_query_status": ([C.c_int, C.c_void_p, C.POINTER(C.c_uint32)], C.c_int),
     "skv_clear_status": ([C.c_int, C.c_void_p], C.c_int),
     "skv_host_alloc": ([C.c_uint64, C.POINTER(C.c_void_p)], C.c_int),
@@ -140,6 +142,16 @@ def copy(segs: list, engine: int = COPY_AUTO, stream=None) -> None:
         chunk = segs[i:i + MAX_SEGMENTS]
         arr = (Segment * len(chunk))(*chunk)
         check(lib().skv_copy(arr, len(chunk), engine, _stream(stream)))
+
+
+def set_copy_tuning(tma_stages: int, tma_tile_bytes: int, tma_ctas_per_sm: int, vec_ctas_per_sm: int) -> None:
+    check(lib().skv_set_copy_tuning(tma_stages, tma_tile_bytes, tma_ctas_per_sm, vec_ctas_per_sm))
+
+
+def get_copy_tuning() -> tuple:
+    a, b, c, d = C.c_int(), C.c_uint32(), C.c_int(), C.c_int()
+    check(lib().skv_get_copy_tuning(C.byref(a), C.byref(b), C.byref(c), C.byref(d)))
+    return a.value, b.value, c.value, d.value
 
 
 def query_status(device: int, stream=None) -> int:
