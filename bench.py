@@ -370,6 +370,32 @@ def run_single(args, torch) -> None:
     print(json.dumps(line))
 
 
+# ------------------------------------------------------------------------------------------------ N > 1: pairs
+
+def pair_role(rank: int, world: int) -> tuple:
+    """(role, peer, active): even ranks prefill, the next odd rank decodes; an unpaired last rank idles."""
+    pairs = world // 2
+    role = "prefill" if rank % 2 == 0 else "decode"
+    peer = rank + 1 if role == "prefill" else rank - 1
+    return role, peer, rank < 2 * pairs
+
+
+def state_layout(kg: skv.KvGeometry, tokens: int) -> dict:
+    """The decode GPU's per-sequence state arena: GDN rows | ids (16-byte rounded) | completion flag."""
+    ids_off = kg.gdn_bytes
+    flag_off = (ids_off + ((4 * tokens + 15) // 16) * 16 + 255) // 256 * 256
+    total = (flag_off + 256 + 1023) // 1024 * 1024
+    return {"ids": ids_off, "flag": flag_off, "bytes": total}
+
+
+def summarize_pairs(max_elapsed_ms: float, per_step_ms: np.ndarray, pairs: int, seq_bytes: int, steps: int) -> dict:
+    """Whole-job numbers from the max-over-ranks timed region and the per-step max-over-ranks latencies."""
+    value = pairs * seq_bytes * steps / (max_elapsed_ms / 1e3) / 1e9
+    per_pair = seq_bytes / (max_elapsed_ms / steps / 1e3) / 1e9
+    return {"value": value, "per_pair_gbs": per_pair, "ms_per_step": max_elapsed_ms / steps,
+            "p50_ms": float(np.percentile(per_step_ms, 50)), "p99_ms": float(np.percentile(per_step_ms, 99))}
+
+
 def run_pairs(args, torch) -> None:
     import torch.distributed as dist
     from datetime import timedelta
@@ -380,53 +406,47 @@ def run_pairs(args, torch) -> None:
     kg = skv.KvGeometry()
     t = args.tokens
     pairs = world // 2
-    role = "prefill" if rank % 2 == 0 else "decode"
-    active = rank < 2 * pairs
-    peer = rank + 1 if role == "prefill" else rank - 1
+    role, peer, active = pair_role(rank, world)
+    lay = state_layout(kg, t)
     stream = torch.cuda.current_stream()
     sp = stream.cuda_stream
     L = skv.lib()
-    state_bytes = ((kg.gdn_bytes + ((4 * t + 15) // 16) * 16 + 4096 + 1023) // 1024) * 1024
-    handles = [None] * world
+    n_blocks = max(args.pool_blocks, kg.n_qsa * kg.blocks(t))
+    off = skv.image_offsets(kg, t, kg.n_qsa)
+    imported = []
+    mine = None
     if role == "decode" and active:
-        dpool = skv.Pool(local, 4096, kg.block_bytes)            # cudaMalloc'd: IPC-exportable base
-        dstate = skv.Pool(local, 1, state_bytes)                 # gdn rows | ids | completion flag
-        seq = SeqOnGpu(torch, kg, t, 4096, seed=args.seed + 1000 + rank, fill=False, pool=dpool)
-        h_pool = (ctypes.c_uint8 * 64)()
-        h_state = (ctypes.c_uint8 * 64)()
-        skv.check(L.skv_ipc_export(dpool.base, h_pool))
-        skv.check(L.skv_ipc_export(dstate.base, h_state))
+        # cudaMalloc'd allocations (their base addresses are what CUDA IPC exports)
+        dpool = skv.Pool(local, n_blocks, kg.block_bytes)
+        dstate = skv.Pool(local, 1, lay["bytes"])
+        zeros = torch.zeros(lay["bytes"], dtype=torch.uint8, device="cuda")
+        skv.copy([skv.segment(zeros, dstate.base, lay["bytes"])], skv.COPY_VEC)   # flag starts at 0
+        seq = SeqOnGpu(torch, kg, t, n_blocks, seed=args.seed + 1000 + rank, fill=False, pool=dpool)
+        mine = {"pool": skv.ipc_export(dpool.base), "state": skv.ipc_export(dstate.base), "tables": seq.host_tables}
         torch.cuda.synchronize()
-        mine = {"pool": bytes(h_pool), "state": bytes(h_state), "tables": seq.host_tables}
-    else:
-        mine = None
+    handles = [None] * world
     dist.all_gather_object(handles, mine)
-    flag_off = kg.gdn_bytes + ((4 * t + 15) // 16) * 16
-    flag_off = (flag_off + 255) // 256 * 256
     if role == "prefill" and active:
-        src = SeqOnGpu(torch, kg, t, 4096, seed=args.seed + rank, fill=True)
+        src = SeqOnGpu(torch, kg, t, n_blocks, seed=args.seed + rank, fill=True)
         other = handles[peer]
-        pool_ptr, state_ptr = ctypes.c_void_p(), ctypes.c_void_p()
-        skv.check(L.skv_ipc_import(local, (ctypes.c_uint8 * 64).from_buffer_copy(other["pool"]),
-                                   ctypes.byref(pool_ptr)))
-        skv.check(L.skv_ipc_import(local, (ctypes.c_uint8 * 64).from_buffer_copy(other["state"]),
-                                   ctypes.byref(state_ptr)))
+        pool_ptr = skv.ipc_import(local, other["pool"])
+        state_ptr = skv.ipc_import(local, other["state"])
+        imported = [pool_ptr, state_ptr]
         dtables = torch.from_numpy(other["tables"].reshape(-1).copy()).cuda()
-        dps = skv.PooledSequence(kg, skv.Pool(local, 4096, kg.block_bytes, memory=pool_ptr.value), t, kg.n_qsa,
-                                 None, dtables, state_ptr.value, state_ptr.value + kg.gdn_bytes)
-        segs = (skv.kv_segments_pool_to_pool(src.ps, dps, dst_base=pool_ptr.value)
-                + skv.state_segments(src.ps, state_ptr.value, state_ptr.value + kg.gdn_bytes))
+        remote = skv.PooledSequence(kg, skv.Pool(local, n_blocks, kg.block_bytes, memory=pool_ptr), t, kg.n_qsa,
+                                    None, dtables, state_ptr, state_ptr + lay["ids"])
+        segs = (skv.kv_segments_pool_to_pool(src.ps, remote, dst_base=pool_ptr)
+                + skv.state_segments(src.ps, state_ptr, state_ptr + lay["ids"]))
         arr = (skv.Segment * len(segs))(*segs)
-        flag = state_ptr.value + flag_off
+        flag = state_ptr + lay["flag"]
         counter = [0]
 
         def step():
             counter[0] += 1
-            skv.check(L.skv_copy(arr, len(segs), skv.COPY_VEC, sp))
+            skv.check(L.skv_copy(arr, len(segs), skv.COPY_VEC, sp))      # remote 16-byte stores over NVLink
             skv.check(L.skv_signal(flag, counter[0], sp))
     elif role == "decode" and active:
-        flag = dstate.base + flag_off
-        torch.cuda.synchronize()
+        flag = dstate.base + lay["flag"]
         counter = [0]
 
         def step():
@@ -435,67 +455,65 @@ def run_pairs(args, torch) -> None:
     else:
         def step():
             pass
-    if role == "decode" and active:
-        torch.zeros(1, device="cuda")  # context warm
+    skv.clear_status(local)
     dist.barrier()
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
     dist.barrier()
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    per_ev = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
     with Clocks(local) as clk:
-        ev0.record(stream)
-        per_ev[0].record(stream)
+        ev[0].record(stream)
         for i in range(args.steps):
             step()
-            per_ev[i + 1].record(stream)
-        ev1.record(stream)
+            ev[i + 1].record(stream)
         torch.cuda.synchronize()
     dist.barrier()
-    elapsed = ev0.elapsed_time(ev1)
-    per = [per_ev[i].elapsed_time(per_ev[i + 1]) for i in range(args.steps)]
+    per = torch.tensor([ev[i].elapsed_time(ev[i + 1]) for i in range(args.steps)], device="cuda")
     status = skv.query_status(local)
-    tot = torch.tensor([elapsed, float(status != 0)], device="cuda")
-    dist.all_reduce(tot, op=dist.ReduceOp.MAX)
-    lat = torch.tensor(per, device="cuda")
-    gathered = [torch.zeros_like(lat) for _ in range(world)]
-    dist.all_gather(gathered, lat)
-    # parity: the decode side reads its pool back through its own table and compares with the source
-    ok = torch.tensor([1.0], device="cuda")
-    if role == "decode" and active:
-        recv = seq.logical(torch)
-        dist.send(torch.tensor([recv.numel()], device="cuda", dtype=torch.int64), peer)
-        dist.send(recv, peer)
-    elif role == "prefill" and active:
-        n = torch.zeros(1, device="cuda", dtype=torch.int64)
-        dist.recv(n, peer)
-        recv = torch.empty(int(n.item()), dtype=torch.uint8, device="cuda")
-        dist.recv(recv, peer)
-        ok[0] = float(bool(torch.equal(recv.view(-1, kg.page_bytes), src.logical(torch))))
+    red = torch.tensor([ev[0].elapsed_time(ev[args.steps]), float(status != 0)], device="cuda")
+    dist.all_reduce(red, op=dist.ReduceOp.MAX)
+    dist.all_reduce(per, op=dist.ReduceOp.MAX)
+    # parity: the decode side packs what it received (our gather, through ITS table) and ships the image to
+    # its prefill peer, which compares it with the pack of its own source through the SOURCE table
+    ok = torch.ones(1, device="cuda")
+    if active:
+        image = torch.empty(off["total"], dtype=torch.uint8, device="cuda")
+        if role == "decode":
+            local_view = skv.PooledSequence(kg, dpool, t, kg.n_qsa, None, seq.tables, dstate.base,
+                                            dstate.base + lay["ids"])
+            skv.copy(skv.pack_segments(local_view, image), skv.COPY_TMA)
+            torch.cuda.synchronize()
+            dist.send(image, peer)
+        else:
+            got = torch.empty_like(image)
+            dist.recv(got, peer)
+            skv.copy(skv.pack_segments(src.ps, image), skv.COPY_TMA)
+            torch.cuda.synchronize()
+            ok[0] = float(bool(torch.equal(got, image)))
     dist.all_reduce(ok, op=dist.ReduceOp.MIN)
-    total_ms = float(tot[0].item())
-    b = kg.metric_bytes(t)
-    value = pairs * b * args.steps / (total_ms / 1e3) / 1e9
-    all_lat = torch.stack(gathered).max(dim=0).values.cpu().numpy()
-    per_pair = b / (total_ms / args.steps / 1e3) / 1e9
+    res = summarize_pairs(float(red[0].item()), per.cpu().numpy(), pairs, kg.metric_bytes(t), args.steps)
     if rank == 0:
-        line = {"metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
-                "warmup": args.warmup, "ms_per_step": round(total_ms / args.steps, 4),
-                "p50_ms": round(float(np.percentile(all_lat, 50)), 4),
-                "p99_ms": round(float(np.percentile(all_lat, 99)), 4), "higher_is_better": True,
-                "scaling": "weak", "vs_baseline": None, "dtype": "u8", "data": "synthetic",
-                "config": {"workload": f"config 3/5: {pairs} prefill->decode pair(s), one {t}-token sequence per "
-                                       "pair per step pushed over NVLink P2P into independent random slots of the "
-                                       "decode GPU's 4,096-block pool", "tokens": t, "pairs": pairs,
-                           "bytes_per_step_per_pair": b, "l2": "inputs larger than L2", "parallelism": f"{pairs} pairs"},
-                "parity": bool(ok.item() == 1.0) and tot[1].item() == 0, "gpu_launches": args.steps * 2 * pairs,
-                "roofline": {"bound": "nvlink", "achieved": round(per_pair, 1), "peak": NVLINK_PEER_COPY_GBS,
-                             "unit": "GB/s", "frac": round(per_pair / NVLINK_PEER_COPY_GBS, 4),
+        line = {"metric": METRIC, "value": round(res["value"], 3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": round(res["ms_per_step"], 4), "p50_ms": round(res["p50_ms"], 4),
+                "p99_ms": round(res["p99_ms"], 4), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                "dtype": "u8", "data": "synthetic",
+                "config": {"workload": f"config 3/5: {pairs} prefill->decode pair(s), one {t}-token sequence per pair "
+                                       "per step pushed over NVLink P2P (CUDA IPC peer pointers) into independent "
+                                       f"random slots of the decode GPU's {n_blocks}-block pool", "tokens": t,
+                           "pairs": pairs, "bytes_per_step_per_pair": kg.metric_bytes(t),
+                           "l2": "inputs larger than L2", "parallelism": f"{pairs} prefill/decode pairs"},
+                "parity": bool(ok.item() == 1.0) and red[1].item() == 0, "gpu_launches": args.steps * 3 * pairs,
+                "roofline": {"bound": "nvlink", "achieved": round(res["per_pair_gbs"], 1), "peak": NVLINK_PEER_COPY_GBS,
+                             "unit": "GB/s", "frac": round(res["per_pair_gbs"] / NVLINK_PEER_COPY_GBS, 4),
                              "peak_kind": "measured peer copy per direction (profiling recipe); 900 nominal",
                              "traffic": None, "kernel": "copy_vec_kernel"},
                 "clocks": clk.summary()}
         print(json.dumps(line))
+    torch.cuda.synchronize()
+    dist.barrier()
+    for p in imported:
+        skv.ipc_close(p)
     dist.barrier()
     dist.destroy_process_group()
 

@@ -174,6 +174,33 @@ def resume(segs: list, mode: int, staging=None, staging_bytes: int = 0, stream=N
     check(lib().skv_resume(arr, len(segs), mode, _ptr(staging), staging_bytes, _stream(stream)))
 
 
+def ipc_export(dev_ptr: int) -> bytes:
+    """The 64-byte CUDA IPC handle of a cudaMalloc'd allocation (its base address)."""
+    h = (C.c_uint8 * 64)()
+    check(lib().skv_ipc_export(dev_ptr, C.cast(h, C.c_void_p)))
+    return bytes(h)
+
+
+def ipc_import(device: int, handle: bytes) -> int:
+    """Open a peer process's allocation on `device`; returns the mapped base address."""
+    h = (C.c_uint8 * 64).from_buffer_copy(handle)
+    out = C.c_void_p()
+    check(lib().skv_ipc_import(device, C.cast(h, C.c_void_p), C.byref(out)))
+    return out.value
+
+
+def ipc_close(ptr: int) -> None:
+    check(lib().skv_ipc_close(ptr))
+
+
+def signal(flag: int, value: int, stream=None) -> None:
+    check(lib().skv_signal(flag, value, _stream(stream)))
+
+
+def wait_flag(flag: int, value: int, timeout_ns: int, stream=None) -> None:
+    check(lib().skv_wait_flag(flag, value, timeout_ns, _stream(stream)))
+
+
 class HostBuffer:
     """Pinned, device-mapped host memory (skv_host_alloc) with a numpy view."""
 
