@@ -54,6 +54,7 @@ def parse():
     ap.add_argument("--engine", default="tma", choices=["tma", "vec"])
     ap.add_argument("--seed", type=int, default=1)
     ap.add_argument("--pool-blocks", type=int, default=4096, help="slots per pool (the configs use 4,096)")
+    ap.add_argument("--p2p", default="pull", choices=["pull", "push"], help="N > 1: which GPU runs the copy")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     return ap.parse_args()
@@ -138,38 +139,70 @@ class Clocks:
 # ------------------------------------------------------------------------------------------------ workloads
 
 class SeqOnGpu:
-    """One 32K sequence resident in a pool on the current GPU, filled with fp16 N(0,1) K/V, fp32 N(0,0.02)
-    state and uniform ids (torch RNG on the device)."""
+    """One sequence resident in a pool on the current GPU, filled with fp16 N(0,1) K/V, fp32 N(0,0.02) state
+    and uniform ids (torch RNG on the device).
 
-    def __init__(self, torch, kg: skv.KvGeometry, tokens: int, n_blocks: int, seed: int, fill: bool,
-                 pool_mem=None, pool=None):
-        self.kg, self.tokens = kg, tokens
+    ipc=False: the pool and the state are torch tensors (single-process use).
+    ipc=True:  the pool and a state arena (GDN rows | ids | flags, `state_layout`) are cudaMalloc'd by the
+               library, so CUDA IPC can export their base addresses to the peer process."""
+
+    def __init__(self, torch, kg: skv.KvGeometry, tokens: int, n_blocks: int, seed: int, fill: bool, ipc: bool = False):
+        self.kg, self.tokens, self.ipc = kg, tokens, ipc
         dev = torch.cuda.current_device()
-        if pool is None:
-            pool_mem = torch.empty(n_blocks * kg.block_bytes, dtype=torch.uint8, device="cuda")
-            pool = skv.Pool(dev, n_blocks, kg.block_bytes, memory=pool_mem)
-        self.pool_mem, self.pool = pool_mem, pool
-        pool.scramble(seed)
+        gen = torch.Generator(device="cuda").manual_seed(seed)
+        ids_words = ((4 * tokens + 15) // 16) * 4
+        if ipc:
+            lay = state_layout(kg, tokens)
+            self.pool_mem = None
+            self.pool = skv.Pool(dev, n_blocks, kg.block_bytes)
+            self.state = skv.Pool(dev, 1, lay["bytes"])
+            self.gdn, self.ids = self.state.base, self.state.base + lay["ids"]
+            self.flag = self.state.base + lay["flag"]
+            zero = torch.zeros(lay["bytes"], dtype=torch.uint8, device="cuda")
+            skv.copy([skv.segment(zero, self.state.base, lay["bytes"])], skv.COPY_VEC)
+            if fill:
+                chunk = 256 << 20
+                total = n_blocks * kg.block_bytes
+                for at in range(0, total, chunk):
+                    n = min(chunk, total - at)
+                    r = torch.randn(n // 2, generator=gen, device="cuda", dtype=torch.float16)
+                    skv.copy([skv.segment(r, self.pool.base + at, n)], skv.COPY_VEC)
+                    torch.cuda.synchronize()
+                gdn = torch.randn(kg.gdn_bytes // 4, generator=gen, device="cuda") * 0.02
+                ids = torch.randint(0, 151936, (ids_words,), generator=gen, device="cuda", dtype=torch.int32)
+                skv.copy([skv.segment(gdn, self.gdn, kg.gdn_bytes), skv.segment(ids, self.ids, 4 * ids_words)],
+                         skv.COPY_VEC)
+                torch.cuda.synchronize()
+        else:
+            self.pool_mem = torch.empty(n_blocks * kg.block_bytes, dtype=torch.uint8, device="cuda")
+            self.pool = skv.Pool(dev, n_blocks, kg.block_bytes, memory=self.pool_mem)
+            if fill:
+                self.pool_mem.view(torch.float16).copy_(
+                    torch.randn(self.pool_mem.numel() // 2, generator=gen, device="cuda", dtype=torch.float16))
+            self.gdn = (torch.randn(kg.gdn_bytes // 4, generator=gen, device="cuda") * 0.02 if fill
+                        else torch.zeros(kg.gdn_bytes // 4, device="cuda"))
+            self.ids = (torch.randint(0, 151936, (ids_words,), generator=gen, device="cuda", dtype=torch.int32)
+                        if fill else torch.zeros(ids_words, device="cuda", dtype=torch.int32))
+        self.pool.scramble(seed)
         nb = kg.blocks(tokens)
-        self.blocks = np.stack([pool.alloc(nb) for _ in range(kg.n_qsa)])
+        self.blocks = np.stack([self.pool.alloc(nb) for _ in range(kg.n_qsa)])
         self.host_tables = skv.PooledSequence.host_tables(kg, self.blocks)
         self.tables = torch.from_numpy(self.host_tables.reshape(-1).copy()).cuda()
-        gen = torch.Generator(device="cuda").manual_seed(seed)
-        if fill and pool_mem is not None:
-            pool_mem.view(torch.float16).copy_(
-                torch.randn(pool_mem.numel() // 2, generator=gen, device="cuda", dtype=torch.float16))
-        self.gdn = (torch.randn(kg.gdn_bytes // 4, generator=gen, device="cuda") * 0.02 if fill
-                    else torch.zeros(kg.gdn_bytes // 4, device="cuda"))
-        ids_words = ((4 * tokens + 15) // 16) * 4
-        self.ids = (torch.randint(0, 151936, (ids_words,), generator=gen, device="cuda", dtype=torch.int32) if fill
-                    else torch.zeros(ids_words, device="cuda", dtype=torch.int32))
-        self.ps = skv.PooledSequence(kg, pool, tokens, kg.n_qsa, self.blocks, self.tables, self.gdn, self.ids)
+        self.ps = skv.PooledSequence(kg, self.pool, tokens, kg.n_qsa, self.blocks, self.tables, self.gdn, self.ids)
 
     def logical(self, torch):
         """Every layer's K/V pages read back through this sequence's own table (for the parity check)."""
         pages = self.kg.pages(self.tokens)
         tab = self.tables.view(self.kg.n_qsa, 2, -1)[:, :, :pages].long().reshape(-1)
         return self.pool_mem.view(-1, self.kg.page_bytes)[tab]
+
+    def packed(self, torch):
+        """The whole sequence packed through its table by the gather kernel (K/V, GDN rows, ids)."""
+        off = skv.image_offsets(self.kg, self.tokens, self.kg.n_qsa)
+        image = torch.zeros(off["total"], dtype=torch.uint8, device="cuda")
+        skv.copy(skv.pack_segments(self.ps, image), skv.COPY_TMA)
+        torch.cuda.synchronize()
+        return image
 
 
 def percentiles(ms: list) -> tuple:
@@ -397,6 +430,13 @@ def summarize_pairs(max_elapsed_ms: float, per_step_ms: np.ndarray, pairs: int, 
 
 
 def run_pairs(args, torch) -> None:
+    """N/2 prefill->decode pairs.  pull (default): the decode GPU's copy kernel reads the prefill GPU's pool
+    pages over NVLink (TMA bulk loads from peer memory, no multicast) and writes its own pool; push: the
+    prefill GPU's vector kernel stores into the decode GPU's pool.  Either way the destination slots are written
+    directly, with no intermediate contiguous copy.  Protocol per step (flags are 8-byte words, release
+    stores / bounded acquire polls): pull = prefill raises READY on the decode GPU, decode waits READY, pulls,
+    raises DONE on the prefill GPU (whose blocks may then be freed), prefill waits DONE; push = prefill pushes
+    and raises ARRIVED, decode waits ARRIVED."""
     import torch.distributed as dist
     from datetime import timedelta
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
@@ -412,47 +452,57 @@ def run_pairs(args, torch) -> None:
     sp = stream.cuda_stream
     L = skv.lib()
     n_blocks = max(args.pool_blocks, kg.n_qsa * kg.blocks(t))
-    off = skv.image_offsets(kg, t, kg.n_qsa)
-    imported = []
+    pull = args.p2p == "pull"
+    seq = None
     mine = None
-    if role == "decode" and active:
-        # cudaMalloc'd allocations (their base addresses are what CUDA IPC exports)
-        dpool = skv.Pool(local, n_blocks, kg.block_bytes)
-        dstate = skv.Pool(local, 1, lay["bytes"])
-        zeros = torch.zeros(lay["bytes"], dtype=torch.uint8, device="cuda")
-        skv.copy([skv.segment(zeros, dstate.base, lay["bytes"])], skv.COPY_VEC)   # flag starts at 0
-        seq = SeqOnGpu(torch, kg, t, n_blocks, seed=args.seed + 1000 + rank, fill=False, pool=dpool)
-        mine = {"pool": skv.ipc_export(dpool.base), "state": skv.ipc_export(dstate.base), "tables": seq.host_tables}
+    if active:
+        seq = SeqOnGpu(torch, kg, t, n_blocks, seed=args.seed + 1000 * (role == "decode") + rank,
+                       fill=role == "prefill", ipc=True)
+        mine = {"pool": skv.ipc_export(seq.pool.base), "state": skv.ipc_export(seq.state.base),
+                "tables": seq.host_tables}
         torch.cuda.synchronize()
     handles = [None] * world
     dist.all_gather_object(handles, mine)
-    if role == "prefill" and active:
-        src = SeqOnGpu(torch, kg, t, n_blocks, seed=args.seed + rank, fill=True)
+    imported = []
+    step = None
+    if active:
         other = handles[peer]
-        pool_ptr = skv.ipc_import(local, other["pool"])
-        state_ptr = skv.ipc_import(local, other["state"])
-        imported = [pool_ptr, state_ptr]
-        dtables = torch.from_numpy(other["tables"].reshape(-1).copy()).cuda()
-        remote = skv.PooledSequence(kg, skv.Pool(local, n_blocks, kg.block_bytes, memory=pool_ptr), t, kg.n_qsa,
-                                    None, dtables, state_ptr, state_ptr + lay["ids"])
-        segs = (skv.kv_segments_pool_to_pool(src.ps, remote, dst_base=pool_ptr)
-                + skv.state_segments(src.ps, state_ptr, state_ptr + lay["ids"]))
-        arr = (skv.Segment * len(segs))(*segs)
-        flag = state_ptr + lay["flag"]
+        peer_pool = skv.ipc_import(local, other["pool"])
+        peer_state = skv.ipc_import(local, other["state"])
+        imported = [peer_pool, peer_state]
+        peer_flag = peer_state + lay["flag"]
+        peer_tables = torch.from_numpy(other["tables"].reshape(-1).copy()).cuda()
+        peer_seq = skv.PooledSequence(kg, skv.Pool(local, n_blocks, kg.block_bytes, memory=peer_pool), t, kg.n_qsa,
+                                      None, peer_tables, peer_state, peer_state + lay["ids"])
         counter = [0]
+        if pull and role == "decode":
+            segs = skv.kv_segments_pool_to_pool(peer_seq, seq.ps) + skv.state_segments(peer_seq, seq.gdn, seq.ids)
+            arr = (skv.Segment * len(segs))(*segs)
 
-        def step():
-            counter[0] += 1
-            skv.check(L.skv_copy(arr, len(segs), skv.COPY_VEC, sp))      # remote 16-byte stores over NVLink
-            skv.check(L.skv_signal(flag, counter[0], sp))
-    elif role == "decode" and active:
-        flag = dstate.base + lay["flag"]
-        counter = [0]
+            def step():
+                counter[0] += 1
+                skv.check(L.skv_wait_flag(seq.flag, counter[0], 5_000_000_000, sp))    # READY
+                skv.check(L.skv_copy(arr, len(segs), skv.COPY_TMA, sp))              # pull over NVLink
+                skv.check(L.skv_signal(peer_flag, counter[0], sp))                   # DONE
+        elif pull:
+            def step():
+                counter[0] += 1
+                skv.check(L.skv_signal(peer_flag, counter[0], sp))                   # READY
+                skv.check(L.skv_wait_flag(seq.flag, counter[0], 5_000_000_000, sp))  # DONE
+        elif role == "prefill":
+            segs = (skv.kv_segments_pool_to_pool(seq.ps, peer_seq, dst_base=peer_pool)
+                    + skv.state_segments(seq.ps, peer_state, peer_state + lay["ids"]))
+            arr = (skv.Segment * len(segs))(*segs)
 
-        def step():
-            counter[0] += 1
-            skv.check(L.skv_wait_flag(flag, counter[0], 5_000_000_000, sp))
-    else:
+            def step():
+                counter[0] += 1
+                skv.check(L.skv_copy(arr, len(segs), skv.COPY_VEC, sp))              # remote 16-byte stores
+                skv.check(L.skv_signal(peer_flag, counter[0], sp))                   # ARRIVED
+        else:
+            def step():
+                counter[0] += 1
+                skv.check(L.skv_wait_flag(seq.flag, counter[0], 5_000_000_000, sp))  # ARRIVED
+    if step is None:
         def step():
             pass
     skv.clear_status(local)
@@ -474,22 +524,16 @@ def run_pairs(args, torch) -> None:
     red = torch.tensor([ev[0].elapsed_time(ev[args.steps]), float(status != 0)], device="cuda")
     dist.all_reduce(red, op=dist.ReduceOp.MAX)
     dist.all_reduce(per, op=dist.ReduceOp.MAX)
-    # parity: the decode side packs what it received (our gather, through ITS table) and ships the image to
-    # its prefill peer, which compares it with the pack of its own source through the SOURCE table
+    # parity: each side packs its copy through ITS OWN table with the gather kernel; the decode side ships
+    # its image to the prefill side, which compares it with the image of the source
     ok = torch.ones(1, device="cuda")
     if active:
-        image = torch.empty(off["total"], dtype=torch.uint8, device="cuda")
+        image = seq.packed(torch)
         if role == "decode":
-            local_view = skv.PooledSequence(kg, dpool, t, kg.n_qsa, None, seq.tables, dstate.base,
-                                            dstate.base + lay["ids"])
-            skv.copy(skv.pack_segments(local_view, image), skv.COPY_TMA)
-            torch.cuda.synchronize()
             dist.send(image, peer)
         else:
             got = torch.empty_like(image)
             dist.recv(got, peer)
-            skv.copy(skv.pack_segments(src.ps, image), skv.COPY_TMA)
-            torch.cuda.synchronize()
             ok[0] = float(bool(torch.equal(got, image)))
     dist.all_reduce(ok, op=dist.ReduceOp.MIN)
     res = summarize_pairs(float(red[0].item()), per.cpu().numpy(), pairs, kg.metric_bytes(t), args.steps)
@@ -499,15 +543,16 @@ def run_pairs(args, torch) -> None:
                 "p99_ms": round(res["p99_ms"], 4), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
                 "dtype": "u8", "data": "synthetic",
                 "config": {"workload": f"config 3/5: {pairs} prefill->decode pair(s), one {t}-token sequence per pair "
-                                       "per step pushed over NVLink P2P (CUDA IPC peer pointers) into independent "
-                                       f"random slots of the decode GPU's {n_blocks}-block pool", "tokens": t,
-                           "pairs": pairs, "bytes_per_step_per_pair": kg.metric_bytes(t),
+                                       f"per step moved over NVLink ({args.p2p}: CUDA IPC peer pointers) straight "
+                                       f"into independent random slots of the decode GPU's {n_blocks}-block pool",
+                           "tokens": t, "pairs": pairs, "p2p": args.p2p, "bytes_per_step_per_pair": kg.metric_bytes(t),
                            "l2": "inputs larger than L2", "parallelism": f"{pairs} prefill/decode pairs"},
-                "parity": bool(ok.item() == 1.0) and red[1].item() == 0, "gpu_launches": args.steps * 3 * pairs,
+                "parity": bool(ok.item() == 1.0) and red[1].item() == 0, "gpu_launches": args.steps * (4 if pull else 3) * pairs,
                 "roofline": {"bound": "nvlink", "achieved": round(res["per_pair_gbs"], 1), "peak": NVLINK_PEER_COPY_GBS,
                              "unit": "GB/s", "frac": round(res["per_pair_gbs"] / NVLINK_PEER_COPY_GBS, 4),
+                             "frac_of_nominal_900": round(res["per_pair_gbs"] / 900.0, 4),
                              "peak_kind": "measured peer copy per direction (profiling recipe); 900 nominal",
-                             "traffic": None, "kernel": "copy_vec_kernel"},
+                             "traffic": None, "kernel": "copy_tma_kernel" if pull else "copy_vec_kernel"},
                 "clocks": clk.summary()}
         print(json.dumps(line))
     torch.cuda.synchronize()
