@@ -1,0 +1,29 @@
+"""The reference's own test programs, compiled UNCHANGED against this build's drop-in headers and sources.
+
+oracle/Makefile builds them from the reference tree (which only the build host has) into oracle/_ref/, mapping
+the reference's include paths onto include/strata_kv/ through oracle/shim/.  Each program is the reference's
+check-and-exit suite; passing it means the drop-in behaves as the reference's own tests require:
+  conversation_cache_test   ConversationCache / ConversationBuffer / the prefix rules   (4,282 checks)
+  conv_cache_test           the checkpoint-chain policy against the parked-conversation cache
+  saved_conv_wire_test      the SR4H codec: layout, round trips, ~30 surgical refusals, slot sinks (483 checks)
+"""
+import os
+import subprocess
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+BIN = os.path.join(ROOT, "oracle", "_ref")
+
+
+@pytest.mark.parametrize("name,expect", [("ref_conversation_cache_test", "4282 checks passed"),
+                                         ("ref_conv_cache_test", "PASS"),
+                                         ("ref_saved_conv_wire_test", "483 checks passed")])
+def test_reference_suite_passes_against_the_drop_in(name, expect):
+    path = os.path.join(BIN, name)
+    if not os.path.exists(path):
+        pytest.skip(f"{name} not built (the reference tree was not present at build time)")
+    r = subprocess.run([path], capture_output=True, text=True, timeout=300,
+                       env=dict(os.environ, CUDA_VISIBLE_DEVICES=""))
+    assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-2000:]
+    assert expect in r.stdout
