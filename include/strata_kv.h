@@ -4,7 +4,7 @@
  * reference's path does with cudaMemcpy (src/core/conversation_snapshot.cpp:105-113, 139-219;
  * src/core/conversation_state.cpp:33-40, 228-267) and with its block movers
  * (src/kernels/cuda/kv_stream.cu:160-252) goes through the entry points below.  The C++ drop-in layer
- * (include/strata_kv/*.hpp, same names and signatures as the reference's conversation_* API) is built on
+ * (the headers under include/strata_kv/, same names and signatures as the reference's conversation_* API) is built on
  * them, and so are the Python bindings used by the tests and bench.py.
  *
  * Conventions

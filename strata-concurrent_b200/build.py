@@ -19,6 +19,12 @@ INCLUDE = os.path.join(ROOT, "include")
 LIB = os.path.join(HERE, "libstrata_kv.so")
 
 CUDA_SOURCES = ["skv_copy.cu", "skv_abi.cu"]
+# the C++ drop-in layer (strata::core API), host code on top of the C ABI
+HOST_SOURCES = ["host/pinned.cpp", "host/transfer.cpp", "host/conversation_snapshot.cpp", "host/conversation_state.cpp",
+                "host/conversation_wire.cpp"]
+CXX = os.environ.get("CXX", "g++")
+CXXFLAGS = ["-std=c++20", "-O2", "-fPIC", "-Wall", "-Wextra", "-Wno-unused-parameter", "-I", INCLUDE, "-I", CSRC,
+            "-I", "/usr/local/cuda/include"]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC,-O2,-fvisibility=hidden",
@@ -38,7 +44,8 @@ def _run(cmd: list[str]) -> None:
 
 
 def build(force: bool = False, verbose_ptxas: bool = False) -> str:
-    deps = [os.path.join(CSRC, f) for f in os.listdir(CSRC)] + [os.path.join(INCLUDE, "strata_kv.h")]
+    deps = [os.path.join(d, f) for d in (CSRC, os.path.join(CSRC, "host"), os.path.join(INCLUDE, "strata_kv"))
+            for f in os.listdir(d)] + [os.path.join(INCLUDE, "strata_kv.h")]
     if not force and not _newer(LIB, deps):
         return LIB
     objs = []
@@ -48,6 +55,10 @@ def build(force: bool = False, verbose_ptxas: bool = False) -> str:
         if verbose_ptxas:
             cmd.insert(1, "-Xptxas=-v")
         _run(cmd)
+        objs.append(obj)
+    for src in HOST_SOURCES:
+        obj = os.path.join(CSRC, src.replace("/", "_").replace(".cpp", ".o"))
+        _run([CXX, *CXXFLAGS, "-c", os.path.join(CSRC, src), "-o", obj])
         objs.append(obj)
     _run([NVCC, *ARCH, "-shared", "-o", LIB, *objs, "-lcudart"])
     for o in objs:

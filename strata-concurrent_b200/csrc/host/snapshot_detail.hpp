@@ -1,0 +1,38 @@
+// snapshot_detail.hpp - shared pieces of the snapshot layer (internal to libstrata_kv.so).
+#pragma once
+
+#include "strata_kv/conversation_snapshot.hpp"
+#include "transfer.hpp"
+
+#include <array>
+#include <initializer_list>
+#include <string>
+
+namespace strata::core::snapshot_detail {
+
+bool fail(std::string& error, const char* message);
+bool checked_product(size_t& out, std::initializer_list<uint64_t> factors);
+bool checked_add(size_t& total, size_t n);
+
+/// One layer's snapshot extents: cells (whole pages up to `upto`), indexer rows, and the byte size of each of
+/// the five streams k, v, k_scale, v_scale, pooled.
+struct LayerExtent {
+    int format = 0;
+    int64_t cells = 0, pooled_rows = 0, page_size = 0;
+    std::array<size_t, 5> bytes{};
+};
+bool layer_extent(const QsaState& st, const ModelGeometry& g, int64_t upto, bool index, LayerExtent& x,
+                  std::string& error);
+bool layer_usable(const QsaState& st, const LayerExtent& x, int64_t upto, std::string& error);
+/// The authoritative source/target of each stream (device pools in mode 0, host pools otherwise).
+std::array<const void*, 5> layer_sources(const QsaState& st);
+/// Stream `i` of a layer as the copy kernels address it (paged through page_table for the K/V streams).
+strata::kv::DeviceStream layer_stream(const QsaState& st, const LayerExtent& x, int i, const void* base);
+
+/// Queue one layer's save / restore into a batch (validation happens here, before anything is queued).
+bool enqueue_kv_save(ConversationKv& image, const QsaState& st, const ModelGeometry& g, int64_t upto, bool index,
+                     strata::kv::Transfer& t, std::string& error, int64_t unchanged, size_t* reused_bytes);
+bool enqueue_kv_restore(const ConversationKv& image, const QsaState& st, const ModelGeometry& g, int64_t upto,
+                        bool index, strata::kv::Transfer& t, std::string& error);
+
+}  // namespace strata::core::snapshot_detail

@@ -1,0 +1,72 @@
+// transfer.hpp - batched device <-> host moves for the snapshot layer (internal to libstrata_kv.so).
+//
+// A Transfer collects items - one logical byte range of a device stream (paged through a page table, or
+// contiguous) paired with host memory (a ConversationBuffer's segments or a contiguous array) - and runs them as
+// ONE batch on the device's legacy stream:
+//   save:    one gather launch (skv_copy) device streams -> device staging image, then one cudaMemcpyAsync per
+//            host piece staging -> host, then one synchronisation and a status-word check;
+//   restore: one cudaMemcpyAsync per host piece host -> staging, then one scatter launch, then the same.
+// The staging image is a per-device buffer kept between calls and grown on demand.
+#pragma once
+
+#include "strata_kv/conversation_buffer.hpp"
+
+#include <cstdint>
+#include <string>
+#include <vector>
+
+namespace strata::kv {
+
+/// A device byte stream: logical byte b lives at base + pages[b / page_bytes] * page_bytes + b % page_bytes, or at
+/// base + b when `pages` is null.
+struct DeviceStream {
+    const void* base = nullptr;
+    const int32_t* pages = nullptr;   // device int32 page table
+    uint32_t page_bytes = 0;
+    int64_t page_limit = 0;           // pages addressable from base
+};
+
+class Transfer {
+public:
+    /// Device stream bytes [from, to) -> the same range of `dst` (already sized to at least `to`).
+    void save(const DeviceStream& src, uint64_t from, uint64_t to, strata::core::ConversationBuffer& dst);
+    /// Device stream bytes [from, to) -> host array `dst` (dst[0] receives byte `from`).
+    void save(const DeviceStream& src, uint64_t from, uint64_t to, uint8_t* dst);
+    /// Host bytes -> device stream bytes [from, to).
+    void restore(const strata::core::ConversationBuffer& src, uint64_t from, uint64_t to, const DeviceStream& dst);
+    void restore(const uint8_t* src, uint64_t from, uint64_t to, const DeviceStream& dst);
+    /// Host -> host copy run in the same batch (a streamed layer's authoritative host pool).
+    void host_copy(const uint8_t* src, uint64_t from, uint64_t to, strata::core::ConversationBuffer& dst);
+
+    bool empty() const { return items_.empty() && host_.empty(); }
+    size_t items() const { return items_.size(); }
+
+    /// Run everything queued (saves and restores may not be mixed in one batch).  On failure `error` names the
+    /// reason; a restore that failed after its first write has left partial state.
+    bool run(std::string& error, const char* what);
+
+private:
+    struct Piece {
+        uint8_t* host;
+        uint64_t rel;   // offset inside the item's range
+        uint64_t bytes;
+    };
+    struct Item {
+        DeviceStream dev;
+        uint64_t from = 0, to = 0;
+        bool save = true;
+        std::vector<Piece> pieces;
+    };
+    struct HostCopy {
+        const uint8_t* src;
+        uint64_t from, to;
+        strata::core::ConversationBuffer* dst;
+    };
+    std::vector<Item> items_;
+    std::vector<HostCopy> host_;
+};
+
+/// Bytes of the per-device staging image currently held (for tests and telemetry).
+uint64_t transfer_staging_bytes(int device);
+
+}  // namespace strata::kv
