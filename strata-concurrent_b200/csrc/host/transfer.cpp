@@ -117,12 +117,29 @@ bool Transfer::run(std::string& error, const char* what) {
         });
         if (!ok) return false;
     }
-    if (!items_.empty()) {
+    // Contiguous items that are not 16-byte granular (a 4-byte block position, say) cannot go through the copy
+    // kernels without touching bytes outside their buffer; the copy engine moves them directly.
+    std::vector<const Item*> kernel_items, direct_items;
+    bool launched = false;
+    for (const Item& it : items_) {
+        const uintptr_t at = reinterpret_cast<uintptr_t>(static_cast<const uint8_t*>(it.dev.base) + it.from);
+        const bool granular = ((at | (it.to - it.from)) & 15u) == 0;
+        if (it.dev.pages || granular) kernel_items.push_back(&it);
+        else direct_items.push_back(&it);
+    }
+    for (const Item* it : direct_items)
+        for (const Piece& p : it->pieces) {
+            uint8_t* dev = const_cast<uint8_t*>(static_cast<const uint8_t*>(it->dev.base)) + it->from + p.rel;
+            const cudaError_t e = it->save ? cudaMemcpyAsync(p.host, dev, p.bytes, cudaMemcpyDeviceToHost, stream)
+                                           : cudaMemcpyAsync(dev, p.host, p.bytes, cudaMemcpyHostToDevice, stream);
+            if (!cuda_ok(e, error, what, "running-state copy")) return false;
+        }
+    if (!kernel_items.empty()) {
         uint64_t total = 0;
-        std::vector<uint64_t> off(items_.size());
-        for (size_t i = 0; i < items_.size(); ++i) {
+        std::vector<uint64_t> off(kernel_items.size());
+        for (size_t i = 0; i < kernel_items.size(); ++i) {
             off[i] = total;
-            total += round256(items_[i].to - items_[i].from);
+            total += round256(kernel_items[i]->to - kernel_items[i]->from);
         }
         uint8_t* staging = nullptr;
         if (!staging_for(total, &staging, error, what)) return false;
@@ -133,9 +150,9 @@ bool Transfer::run(std::string& error, const char* what) {
             return false;
         }
         std::vector<skv_segment> segs;
-        segs.reserve(items_.size());
-        for (size_t i = 0; i < items_.size(); ++i) {
-            const Item& it = items_[i];
+        segs.reserve(kernel_items.size());
+        for (size_t i = 0; i < kernel_items.size(); ++i) {
+            const Item& it = *kernel_items[i];
             skv_segment s{};
             uint8_t* stage = staging + off[i];
             const uint8_t* base = static_cast<const uint8_t*>(it.dev.base);
@@ -175,8 +192,8 @@ bool Transfer::run(std::string& error, const char* what) {
             return true;
         };
         auto host_moves = [&](bool to_host) -> bool {
-            for (size_t i = 0; i < items_.size(); ++i)
-                for (const Piece& p : items_[i].pieces) {
+            for (size_t i = 0; i < kernel_items.size(); ++i)
+                for (const Piece& p : kernel_items[i]->pieces) {
                     uint8_t* stage = staging + off[i] + p.rel;
                     const cudaError_t e =
                         to_host ? cudaMemcpyAsync(p.host, stage, p.bytes, cudaMemcpyDeviceToHost, stream)
@@ -190,9 +207,10 @@ bool Transfer::run(std::string& error, const char* what) {
         } else {
             if (!host_moves(false) || !launch()) return false;
         }
+        launched = true;
     }
     if (!cuda_ok(cudaStreamSynchronize(stream), error, what, "synchronize")) return false;
-    if (!items_.empty()) {
+    if (launched) {   // the status word the kernels of this batch reported into
         int dev = -1;
         uint32_t status = 0;
         cudaGetDevice(&dev);

@@ -1,0 +1,44 @@
+"""The C++ drop-in API on a real device (tests/cpp/*.cpp, reference-style check-and-exit programs).
+
+snapshot_gpu_test parks config 1 (full geometry, 4,096 tokens, seed 1) from a pool at seed-random slots with
+conversation_snapshot_save, and the SR4H payload of the parked image must hash to the FNV-1a the reference's own
+save + encode produced from its identity pool (tests/golden/golden.json).  It then mounts the image into a
+differently permuted pool and reads every byte back; see the program's header for the full list.
+"""
+import json
+import os
+import subprocess
+
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+SRC = os.path.join(ROOT, "tests", "cpp")
+BIN = os.path.join(SRC, "bin")
+PKG = os.path.join(ROOT, "strata-concurrent_b200")
+ORACLE = os.path.join(ROOT, "oracle")
+CUDA = "/usr/local/cuda"
+
+
+def build(name: str) -> str:
+    os.makedirs(BIN, exist_ok=True)
+    src = os.path.join(SRC, name + ".cpp")
+    out = os.path.join(BIN, name)
+    deps = [src, os.path.join(PKG, "libstrata_kv.so"), os.path.join(ORACLE, "liboracle.so")]
+    if not os.path.exists(out) or any(os.path.getmtime(d) > os.path.getmtime(out) for d in deps):
+        subprocess.run(["g++", "-std=c++20", "-O2", "-I", os.path.join(ROOT, "include"), "-I", ORACLE,
+                        "-I", f"{CUDA}/include", "-o", out, src, "-L", PKG, "-lstrata_kv", f"-Wl,-rpath,{PKG}",
+                        "-L", ORACLE, "-loracle", f"-Wl,-rpath,{ORACLE}", "-L", f"{CUDA}/lib64", "-lcudart",
+                        f"-Wl,-rpath,{CUDA}/lib64"], check=True)
+    return out
+
+
+def test_snapshot_park_mount_matches_reference_payload(torch_cuda):
+    golden = json.load(open(os.path.join(ROOT, "tests", "golden", "golden.json")))["config1"]
+    exe = build("snapshot_gpu_test")
+    r = subprocess.run([exe, str(golden["bytes"]), str(golden["payload_hash"])], capture_output=True, text=True,
+                       timeout=600)
+    print(r.stdout)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
+    assert "checks passed" in r.stdout
