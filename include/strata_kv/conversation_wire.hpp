@@ -22,6 +22,7 @@
 #pragma once
 
 #include "strata_kv/conversation_cache.hpp"
+#include "strata_kv/fnv.hpp"
 
 #include <array>
 #include <cstddef>
@@ -229,8 +230,5 @@ bool conversation_wire_decode(const uint8_t* data, uint64_t bytes, SavedConversa
 bool conversation_wire_peek(const uint8_t* data, uint64_t bytes, WireHeaderRecord& header, std::string& error);
 uint64_t conversation_wire_payload_hash(const uint8_t* data, uint64_t bytes);
 std::string conversation_wire_describe(const WireHeaderRecord& header);
-
-/// FNV-1a 64 over [p, p + n) continuing from `seed` (the public FNV-1a algorithm).
-uint64_t fnv1a64(const uint8_t* p, uint64_t n, uint64_t seed = kWireHashSeed);
 
 }  // namespace strata::core

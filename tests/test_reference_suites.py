@@ -8,6 +8,9 @@ check-and-exit suite; passing it means the drop-in behaves as the reference's ow
   saved_conv_wire_test      the SR4H codec: layout, round trips, ~30 surgical refusals, slot sinks (483 checks)
   conversation_validation_test   (host-only build) the snapshot layer's refusals before any write, byte
                             estimates, layer carves and split stage sets (1,323 checks; CUDA is never initialised)
+  handoff_arena_test        the hand-off table: on-disk layout, sizing, the claim/publish/release lifecycle,
+                            dead and recycled owners, leases, refusals, cross-process readers, a >1 GiB slot and
+                            an instance restart (268 checks; child processes, a tmpfs arena under /dev/shm)
 """
 import os
 import subprocess
@@ -21,7 +24,8 @@ BIN = os.path.join(ROOT, "oracle", "_ref")
 @pytest.mark.parametrize("name,expect", [("ref_conversation_cache_test", "4282 checks passed"),
                                          ("ref_conv_cache_test", "PASS"),
                                          ("ref_saved_conv_wire_test", "483 checks passed"),
-                                         ("ref_conversation_validation_test", "1323 host-only checks passed")])
+                                         ("ref_conversation_validation_test", "1323 host-only checks passed"),
+                                         ("ref_handoff_arena_test", "268 checks, OK")])
 def test_reference_suite_passes_against_the_drop_in(name, expect):
     path = os.path.join(BIN, name)
     if not os.path.exists(path):
