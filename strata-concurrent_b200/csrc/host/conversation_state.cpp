@@ -13,8 +13,7 @@
 #include <limits>
 
 namespace strata::core {
-namespace {
-using namespace snapshot_detail;
+namespace snapshot_detail {
 
 std::array<int64_t, 18> geometry_key(const ModelGeometry& g) {
     return {g.n_embd,    g.n_layers,       g.qsa_interval,  g.ssm_state_size, g.ssm_k_heads, g.ssm_v_heads,
@@ -22,20 +21,14 @@ std::array<int64_t, 18> geometry_key(const ModelGeometry& g) {
             g.idx_q_heads, g.idx_key_dim,   g.hc,            g.hc_lr,      g.n_expert,    g.n_ff};
 }
 
-/// Make `device` current for a scope (a negative device, or the current one, changes nothing).
-struct DeviceScope {
-    int previous = -1;
-    explicit DeviceScope(int device) {
-        int cur = 0;
-        if (device >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != device && cudaSetDevice(device) == cudaSuccess)
-            previous = cur;
-    }
-    ~DeviceScope() {
-        if (previous >= 0) cudaSetDevice(previous);
-    }
-    DeviceScope(const DeviceScope&) = delete;
-    DeviceScope& operator=(const DeviceScope&) = delete;
-};
+DeviceScope::DeviceScope(int device) {
+    int cur = 0;
+    if (device >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != device && cudaSetDevice(device) == cudaSuccess)
+        previous = cur;
+}
+DeviceScope::~DeviceScope() {
+    if (previous >= 0) cudaSetDevice(previous);
+}
 
 bool device_sync(std::string& error) {
     const cudaError_t e = cudaDeviceSynchronize();
@@ -220,7 +213,9 @@ bool enqueue_checkpoint_save(ConversationCheckpoint& c, const SessionState& ss, 
     return true;
 }
 
-}  // namespace
+}  // namespace snapshot_detail
+
+using namespace snapshot_detail;
 
 // ------------------------------------------------------------------------------------------------ sizes
 

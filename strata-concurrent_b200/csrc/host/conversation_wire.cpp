@@ -7,6 +7,7 @@
 // bytes that actually remain, then the blobs are copied into a fresh image that replaces the caller's only on
 // success.
 #include "strata_kv/conversation_wire.hpp"
+#include "wire_detail.hpp"
 
 #include <algorithm>
 #include <cerrno>
@@ -112,13 +113,17 @@ bool depth_ok(const ConversationCheckpoint& c, int depth, int max_depth) {
     return true;
 }
 
+uint64_t own_size(const void*, uint64_t real) { return real; }
+
 /// Walks the image in record order.  `emit(bytes)` gets each record piece; `blob(buffer)` returns the
-/// absolute payload offset of a buffer's pool entry (0 for an empty one).
+/// absolute payload offset of a buffer's pool entry (0 for an empty one); `size_of(buffer, its size())` gives
+/// the byte count the records carry for it (its own size, or a side table's for a shape image).
 class Traversal {
 public:
     using Emit = std::function<bool(const uint8_t*, size_t)>;
     using BlobOf = std::function<uint64_t(const ConversationBuffer*, const std::vector<uint8_t>*)>;
-    Traversal(Emit emit, BlobOf blob) : emit_(std::move(emit)), blob_(std::move(blob)) {}
+    Traversal(Emit emit, BlobOf blob, const wire_detail::SizeOf& size_of = own_size)
+        : emit_(std::move(emit)), blob_(std::move(blob)), size_of_(size_of) {}
 
     bool body(const SavedConversation& s) {
         for (const auto& k : s.kv)
@@ -141,11 +146,11 @@ private:
         return out(h);
     }
     void ref(Bytes& b, const ConversationBuffer& buf) {
-        b.u64(buf.size());
+        b.u64(size_of_(&buf, buf.size()));
         b.u64(blob_(&buf, nullptr));
     }
     void ref(Bytes& b, const std::vector<uint8_t>& vec) {
-        b.u64(vec.size());
+        b.u64(size_of_(&vec, vec.size()));
         b.u64(blob_(nullptr, &vec));
     }
     bool kv_record(const ConversationKv& k) {
@@ -200,6 +205,7 @@ private:
 
     Emit emit_;
     BlobOf blob_;
+    wire_detail::SizeOf size_of_;
 };
 
 struct Planned {
@@ -207,7 +213,8 @@ struct Planned {
     std::vector<Blob> blobs;
 };
 
-bool plan_image(const SavedConversation& s, int max_depth, Planned& p, std::string& error) {
+bool plan_image(const SavedConversation& s, int max_depth, Planned& p, std::string& error,
+                const wire_detail::SizeOf& size_of = own_size) {
     if (!s.live.stage_parts.empty())
         return refuse(error, "the live checkpoint carries layer-split stage parts; a parked image keeps them in "
                              "SavedConversation::stage_parts (layer-split parking is not supported that way)");
@@ -225,7 +232,7 @@ bool plan_image(const SavedConversation& s, int max_depth, Planned& p, std::stri
             return true;
         },
         [&](const ConversationBuffer* buf, const std::vector<uint8_t>* vec) -> uint64_t {
-            const uint64_t n = buf ? buf->size() : vec->size();
+            const uint64_t n = buf ? size_of(buf, buf->size()) : size_of(vec, vec->size());
             if (!n) return 0;
             const uint64_t rel = align64(pool);
             Blob b{buf, vec, rel, n};
@@ -233,7 +240,8 @@ bool plan_image(const SavedConversation& s, int max_depth, Planned& p, std::stri
             pool = rel;
             overflow |= !add_to(pool, n);
             return 0;
-        });
+        },
+        size_of);
     walk.body(s);
     if (overflow) return refuse(error, "byte count overflow");
     WirePlan& w = p.plan;
@@ -297,6 +305,54 @@ void header_bytes(const SavedConversation& s, const WirePlan& w, const WireIdent
 }
 
 }  // namespace
+
+namespace wire_detail {
+
+bool plan(const SavedConversation& image, int max_depth, const SizeOf& size_of, WirePlan& plan,
+          std::vector<PlannedBlob>& blobs, std::string& error) {
+    Planned p;
+    if (!plan_image(image, max_depth, p, error, size_of)) return false;
+    plan = p.plan;
+    blobs.clear();
+    blobs.reserve(p.blobs.size());
+    for (const Blob& b : p.blobs)
+        blobs.push_back(PlannedBlob{b.buf ? (const void*) b.buf : (const void*) b.vec, b.rel, b.bytes});
+    return true;
+}
+
+bool write_records(const SavedConversation& image, const WireIdentity& identity, const WirePlan& plan,
+                   const std::vector<PlannedBlob>& blobs, const SizeOf& size_of, uint8_t* out, std::string& error) {
+    uint8_t* at = out;
+    header_bytes(image, plan, identity, at);
+    at += kWireHeaderRecordBytes;
+    const uint8_t* end = out + plan.blob_pool_off;
+    size_t next = 0;
+    bool order_ok = true, room = true;
+    Traversal walk(
+        [&](const uint8_t* d, size_t n) {
+            if ((uint64_t) (end - at) < n) return room = false;
+            std::memcpy(at, d, n);
+            at += n;
+            return true;
+        },
+        [&](const ConversationBuffer* buf, const std::vector<uint8_t>* vec) -> uint64_t {
+            const uint64_t n = buf ? size_of(buf, buf->size()) : size_of(vec, vec->size());
+            if (!n) return 0;
+            const void* key = buf ? (const void*) buf : (const void*) vec;
+            if (next >= blobs.size() || blobs[next].key != key) {
+                order_ok = false;
+                return 0;
+            }
+            return plan.blob_pool_off + blobs[next++].rel;
+        },
+        size_of);
+    if (!walk.body(image) || !room) return refuse(error, "internal: the records overran their planned bytes");
+    if (!order_ok || next != blobs.size()) return refuse(error, "internal: the blob order changed between passes");
+    std::memset(at, 0, (size_t) (end - at));
+    return true;
+}
+
+}  // namespace wire_detail
 
 bool conversation_wire_plan(const SavedConversation& image, int max_checkpoint_depth, WirePlan& plan,
                             std::string& error) {

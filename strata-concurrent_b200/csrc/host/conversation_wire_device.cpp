@@ -1,0 +1,411 @@
+// conversation_wire_device.cpp - SR4H payloads packed straight from device state
+// (include/strata_kv/conversation_wire_device.hpp).
+//
+// 1. Validate exactly as conversation_snapshot_save does (conversation_snapshot_bytes).
+// 2. Build a SHAPE image: the SavedConversation that save would produce, with every metadata field real but
+//    every byte buffer empty; a side table maps each buffer to the pieces it is made of (a device stream through
+//    a page table, a contiguous device range, or host memory) and so to its byte count.
+// 3. Plan the payload from the shape (the encoder's own plan pass, sizes from the side table) and write the
+//    header + record stream on the host.
+// 4. Per device: one batch of gather launches moves that device's pieces into a zeroed image of the blob pool
+//    (the staging buffer, or the destination itself when it is device memory), then one device-to-host copy per
+//    run of consecutive pieces; host-resident pieces are copied on the host, sub-16-byte pieces by the copy
+//    engine, and every byte of the pool nobody wrote is zeroed.
+#include "strata_kv/conversation_wire_device.hpp"
+
+#include "snapshot_detail.hpp"
+#include "strata_kv.h"
+#include "wire_detail.hpp"
+
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstring>
+#include <map>
+#include <unordered_map>
+
+namespace strata::core {
+namespace {
+using namespace snapshot_detail;
+
+constexpr int kHostSide = -1;
+
+/// One contiguous part of a blob.
+struct Piece {
+    int device = kHostSide;              // kHostSide: `host` holds the bytes
+    strata::kv::DeviceStream dev;        // device side: logical bytes [from, from + bytes) of this stream
+    uint64_t from = 0;
+    const uint8_t* host = nullptr;
+    uint64_t rel = 0;                    // offset inside the blob
+    uint64_t bytes = 0;
+};
+struct Source {
+    std::vector<Piece> pieces;
+    uint64_t bytes = 0;
+};
+using Side = std::unordered_map<const void*, Source>;
+
+bool pfail(std::string& error, const std::string& why) {
+    error = "conversation wire device pack: " + why;
+    return false;
+}
+bool cuda_ok(cudaError_t e, std::string& error, const char* step) {
+    if (e == cudaSuccess) return true;
+    (void) cudaGetLastError();
+    return pfail(error, std::string(step) + ": " + cudaGetErrorString(e));
+}
+
+void add_device(Side& side, const void* key, int device, const strata::kv::DeviceStream& s, uint64_t from,
+                uint64_t bytes) {
+    if (!bytes) return;
+    Source& src = side[key];
+    src.pieces.push_back(Piece{device, s, from, nullptr, src.bytes, bytes});
+    src.bytes += bytes;
+}
+void add_host(Side& side, const void* key, const uint8_t* p, uint64_t bytes) {
+    if (!bytes) return;
+    Source& src = side[key];
+    src.pieces.push_back(Piece{kHostSide, {}, 0, p, src.bytes, bytes});
+    src.bytes += bytes;
+}
+strata::kv::DeviceStream flat(const void* p) {
+    strata::kv::DeviceStream s;
+    s.base = p;
+    return s;
+}
+
+/// One layer's K/V record and its five streams (the shape twin of enqueue_kv_save, no retained prefix).
+bool shape_kv(ConversationKv& image, const QsaState& st, const ModelGeometry& g, int64_t upto, bool index,
+              int device, Side& side, std::string& error) {
+    LayerExtent x;
+    if (!layer_extent(st, g, upto, index, x, error) || !layer_usable(st, x, upto, error)) return false;
+    image.format = x.format;
+    image.cells = x.cells;
+    image.heads = g.n_head_kv;
+    image.head_dim = g.head_dim;
+    image.page_size = x.page_size;
+    image.pooled_rows = x.pooled_rows;
+    image.idx_dim = g.idx_key_dim;
+    const auto src = layer_sources(st);
+    const ConversationBuffer* dst[5] = {&image.k, &image.v, &image.k_scale, &image.v_scale, &image.pooled};
+    for (int i = 0; i < 5; ++i) {
+        const uint64_t n = x.bytes[(size_t) i];
+        if (!n) continue;
+        if (!src[(size_t) i]) return fail(error, "missing state buffer");
+        if (i < 4 && st.kv_mode != 0)
+            add_host(side, dst[i], static_cast<const uint8_t*>(src[(size_t) i]), n);
+        else
+            add_device(side, dst[i], device, layer_stream(st, x, i, src[(size_t) i]), 0, n);
+    }
+    return true;
+}
+
+/// A session's running state into checkpoint `c` (whose ids are set): the shape twin of enqueue_checkpoint_save.
+bool shape_running(ConversationCheckpoint& c, const SessionState& ss, const ModelGeometry& g, int device, Side& side,
+                   std::string& error) {
+    ConversationStateSizes z;
+    if (!running_targets(ss, g, c.ids.size(), z, error)) return false;
+    add_device(side, &c.gdn, device, flat(ss.gdn_state), 0, z.gdn);
+    if (ss.ple_hist) add_device(side, &c.ple, device, flat(ss.ple_hist), 0, z.ple);
+    for (size_t j = 0; j < owned_count(ss); ++j) {
+        const QsaState& st = owned_layer(ss, j);
+        add_device(side, &c.tails, device, flat(st.idx_tail), 0, z.tail);
+        add_device(side, &c.dead, device, flat(st.idx_dead), 0, z.dead);
+        add_device(side, &c.block_pos, device, flat(st.idx_block_pos), 0, z.block_pos);
+    }
+    return true;
+}
+
+/// A retained checkpoint (host data already): metadata copied, its byte vectors referenced in place.
+void shape_retained(ConversationCheckpoint& out, const ConversationCheckpoint& c, Side& side) {
+    out.ids = c.ids;
+    out.imgs = c.imgs;
+    out.used = c.used;
+    add_host(side, &out.gdn, c.gdn.data(), c.gdn.size());
+    add_host(side, &out.ple, c.ple.data(), c.ple.size());
+    add_host(side, &out.tails, c.tails.data(), c.tails.size());
+    add_host(side, &out.dead, c.dead.data(), c.dead.size());
+    add_host(side, &out.block_pos, c.block_pos.data(), c.block_pos.size());
+    out.stage_parts.resize(c.stage_parts.size());   // sized before any part registers an address
+    for (size_t i = 0; i < c.stage_parts.size(); ++i) shape_retained(out.stage_parts[i], c.stage_parts[i], side);
+}
+
+int resolve(int device) {
+    if (device >= 0) return device;
+    int cur = 0;
+    cudaGetDevice(&cur);
+    return cur;
+}
+
+/// The shape of conversation_snapshot_save's image, in the same order.
+bool build_shape(const ConversationView& view, const SessionState& ss, const ConversationStageSet& stages,
+                 const ModelGeometry& g, const QsaState& draft, SavedConversation& shape, Side& side,
+                 std::string& error) {
+    size_t estimate = 0;
+    if (!conversation_snapshot_bytes(view, ss, stages, g, draft, estimate, error)) return false;
+    shape = SavedConversation{};
+    side.clear();
+    shape.geometry = geometry_key(g);
+    shape.layer_lo = ss.layer_lo;
+    shape.layer_hi = ss.layer_hi;
+    shape.live.ids = view.ids;
+    shape.live.imgs = view.images;
+    shape.cvec = view.cvec;
+    shape.checkpoints.resize(view.checkpoints.size());
+    for (size_t i = 0; i < view.checkpoints.size(); ++i) shape_retained(shape.checkpoints[i], view.checkpoints[i], side);
+    const size_t layers = owned_count(ss);
+    shape.kv.resize(layers + 1);
+    const int64_t upto = (int64_t) view.ids.size();
+    const int main_dev = resolve(stages.main_device);
+    if (!shape_running(shape.live, ss, g, main_dev, side, error)) return false;
+    for (size_t j = 0; j < layers; ++j)
+        if (!shape_kv(shape.kv[j], owned_layer(ss, j), g, upto, true, main_dev, side, error)) return false;
+    const int draft_dev = stages.empty() ? main_dev : resolve(stages.draft_device);
+    if (!shape_kv(shape.kv.back(), draft, g, upto, false, draft_dev, side, error)) return false;
+    shape.stage_parts.resize((size_t) stage_count(stages));
+    for (int64_t i = 0; i < stage_count(stages); ++i) {
+        const ConversationStage& stage = stages.stages[i];
+        const SessionState& sss = *stage.session;
+        ConversationStageSnapshot& part = shape.stage_parts[(size_t) i];
+        part.layer_lo = sss.layer_lo;
+        part.layer_hi = sss.layer_hi;
+        part.state.ids = view.ids;
+        part.kv.resize(owned_count(sss));
+        const int dev = resolve(stage.device);
+        if (!shape_running(part.state, sss, g, dev, side, error)) return false;
+        for (size_t j = 0; j < part.kv.size(); ++j)
+            if (!shape_kv(part.kv[j], owned_layer(sss, j), g, upto, true, dev, side, error)) return false;
+    }
+    return true;
+}
+
+wire_detail::SizeOf side_sizes(const Side& side) {
+    return [&side](const void* key, uint64_t real) -> uint64_t {
+        const auto it = side.find(key);
+        return it == side.end() ? real : it->second.bytes;
+    };
+}
+
+/// A piece placed at its absolute payload offset.
+struct Placed {
+    const Piece* piece;
+    uint64_t at;
+};
+
+bool granular(const Piece& p, uint64_t at) {
+    if (p.dev.pages) return true;   // paged streams are page-granular by construction
+    const uintptr_t src = reinterpret_cast<uintptr_t>(static_cast<const uint8_t*>(p.dev.base) + p.from);
+    return ((src | at | p.bytes) & 15u) == 0;
+}
+
+skv_segment segment_of(const Piece& p, uint8_t* dst) {
+    skv_segment s{};
+    const uint8_t* base = static_cast<const uint8_t*>(p.dev.base);
+    s.bytes = p.bytes;
+    s.dst = dst;
+    if (p.dev.pages) {
+        s.src = base;
+        s.src_pages = p.dev.pages + p.from / p.dev.page_bytes;
+        s.page_bytes = p.dev.page_bytes;
+        s.src_page_limit = p.dev.page_limit;
+    } else {
+        s.src = base + p.from;
+    }
+    return s;
+}
+
+bool launch_all(const std::vector<skv_segment>& segs, std::string& error) {
+    for (size_t i = 0; i < segs.size(); i += SKV_COPY_MAX_SEGMENTS) {
+        const int n = (int) std::min<size_t>(SKV_COPY_MAX_SEGMENTS, segs.size() - i);
+        if (skv_copy(segs.data() + i, n, SKV_COPY_AUTO, nullptr) != SKV_OK)
+            return pfail(error, std::string("gather: ") + skv_last_error());
+    }
+    return true;
+}
+
+bool status_clean(int device, std::string& error) {
+    uint32_t status = 0;
+    if (skv_query_status(device, nullptr, &status) != SKV_OK) return pfail(error, skv_last_error());
+    if (status) return pfail(error, "the device refused part of the gather (a page-table entry outside its pool)");
+    return true;
+}
+
+}  // namespace
+
+// ------------------------------------------------------------------------------------------------ public API
+
+bool conversation_wire_pack_plan(const ConversationView& view, const SessionState& ss,
+                                 const ConversationStageSet& stages, const ModelGeometry& g, const QsaState& draft,
+                                 WirePlan& plan, std::string& error, const WireDeviceOptions& opt) {
+    SavedConversation shape;
+    Side side;
+    std::vector<wire_detail::PlannedBlob> blobs;
+    return build_shape(view, ss, stages, g, draft, shape, side, error) &&
+           wire_detail::plan(shape, opt.max_checkpoint_depth, side_sizes(side), plan, blobs, error);
+}
+
+bool conversation_wire_pack_plan(const ConversationView& view, const SessionState& ss, const ModelGeometry& g,
+                                 const QsaState& draft, WirePlan& plan, std::string& error,
+                                 const WireDeviceOptions& opt) {
+    return conversation_wire_pack_plan(view, ss, {}, g, draft, plan, error, opt);
+}
+
+bool conversation_wire_pack_device(const ConversationView& view, const SessionState& ss,
+                                   const ConversationStageSet& stages, const ModelGeometry& g, const QsaState& draft,
+                                   const WireIdentity& identity, uint8_t* dst, uint64_t capacity, WirePlan& plan,
+                                   WireEncoded& out, std::string& error, const WireDeviceOptions& opt) {
+    SavedConversation shape;
+    Side side;
+    std::vector<wire_detail::PlannedBlob> blobs;
+    if (!build_shape(view, ss, stages, g, draft, shape, side, error)) return false;
+    const wire_detail::SizeOf sizes = side_sizes(side);
+    WirePlan p;
+    if (!wire_detail::plan(shape, opt.max_checkpoint_depth, sizes, p, blobs, error)) return false;
+    if (!dst) return pfail(error, "no destination");
+    if (capacity < p.total_bytes)
+        return pfail(error, "the payload needs " + std::to_string(p.total_bytes) + " bytes; the destination holds " +
+                                std::to_string(capacity));
+    cudaPointerAttributes attr{};
+    if (!cuda_ok(cudaPointerGetAttributes(&attr, dst), error, "destination attributes")) return false;
+    const bool on_device = attr.type == cudaMemoryTypeDevice;
+    const int dst_device = on_device ? attr.device : kHostSide;
+
+    // every piece at its absolute offset, in payload order
+    std::vector<Placed> placed;
+    for (const auto& b : blobs) {
+        const auto it = side.find(b.key);
+        if (it == side.end()) return pfail(error, "internal: a planned blob has no source");
+        for (const Piece& pc : it->second.pieces) placed.push_back(Placed{&pc, p.blob_pool_off + b.rel + pc.rel});
+    }
+    std::map<int, std::vector<size_t>> by_device;   // kernel-gathered pieces per device
+    std::vector<size_t> direct, host;
+    for (size_t i = 0; i < placed.size(); ++i) {
+        const Piece& pc = *placed[i].piece;
+        if (pc.device == kHostSide) host.push_back(i);
+        else if (granular(pc, placed[i].at)) by_device[pc.device].push_back(i);
+        else direct.push_back(i);
+        if (on_device && pc.device != kHostSide && pc.device != dst_device)
+            return pfail(error, "a device destination must be on the device of every device-resident blob (blob on " +
+                                    std::to_string(pc.device) + ", destination on " + std::to_string(dst_device) + ")");
+    }
+
+    // header + records
+    std::vector<uint8_t> records;
+    uint8_t* rec = dst;
+    if (on_device) {
+        records.resize((size_t) p.blob_pool_off);
+        rec = records.data();
+    }
+    if (!wire_detail::write_records(shape, identity, p, blobs, sizes, rec, error)) return false;
+
+    if (on_device) {
+        const DeviceScope on(dst_device);
+        if (!device_sync(error)) return false;   // the session's producers are done before the reads
+        if (!cuda_ok(cudaMemsetAsync(dst + p.blob_pool_off, 0, p.blob_pool_bytes, nullptr), error, "pool clear") ||
+            !cuda_ok(cudaMemcpyAsync(dst, records.data(), records.size(), cudaMemcpyHostToDevice, nullptr), error,
+                     "records"))
+            return false;
+        if (skv_clear_status(dst_device, nullptr) != SKV_OK) return pfail(error, skv_last_error());
+        std::vector<skv_segment> segs;
+        for (size_t i : by_device[dst_device]) segs.push_back(segment_of(*placed[i].piece, dst + placed[i].at));
+        if (!launch_all(segs, error)) return false;
+        for (size_t i : direct) {
+            const Piece& pc = *placed[i].piece;
+            if (!cuda_ok(cudaMemcpyAsync(dst + placed[i].at, static_cast<const uint8_t*>(pc.dev.base) + pc.from,
+                                         pc.bytes, cudaMemcpyDeviceToDevice, nullptr),
+                         error, "running-state copy"))
+                return false;
+        }
+        for (size_t i : host) {
+            const Piece& pc = *placed[i].piece;
+            if (!cuda_ok(cudaMemcpyAsync(dst + placed[i].at, pc.host, pc.bytes, cudaMemcpyHostToDevice, nullptr),
+                         error, "host blob copy"))
+                return false;
+        }
+        if (!cuda_ok(cudaStreamSynchronize(nullptr), error, "synchronize") ||
+            (!segs.empty() && !status_clean(dst_device, error)))
+            return false;
+        plan = p;
+        out.bytes = p.total_bytes;
+        out.payload_hash = 0;
+        out.blob_pool_bytes = p.blob_pool_bytes;
+        out.blobs = blobs.size();
+        return true;
+    }
+
+    // host destination: mark what each step writes, so every other pool byte is zeroed exactly once
+    std::vector<std::pair<uint64_t, uint64_t>> written;   // [begin, end) absolute
+    for (auto& [device, idx] : by_device) {
+        const DeviceScope on(device);
+        if (!device_sync(error)) return false;
+        const uint64_t lo = placed[idx.front()].at & ~uint64_t(255);
+        const uint64_t hi = placed[idx.back()].at + placed[idx.back()].piece->bytes;
+        uint8_t* staging = nullptr;
+        if (!strata::kv::transfer_staging(hi - lo, &staging, error, "conversation wire device pack")) return false;
+        if (skv_clear_status(device, nullptr) != SKV_OK) return pfail(error, skv_last_error());
+        if (!cuda_ok(cudaMemsetAsync(staging, 0, hi - lo, nullptr), error, "staging clear")) return false;
+        std::vector<skv_segment> segs;
+        segs.reserve(idx.size());
+        for (size_t i : idx) segs.push_back(segment_of(*placed[i].piece, staging + (placed[i].at - lo)));
+        if (!launch_all(segs, error)) return false;
+        // one copy per run: consecutive placed pieces (payload order) that all belong to this device's gather
+        for (size_t k = 0; k < idx.size();) {
+            size_t e = k;
+            while (e + 1 < idx.size() && idx[e + 1] == idx[e] + 1) ++e;
+            const uint64_t a = placed[idx[k]].at, b = placed[idx[e]].at + placed[idx[e]].piece->bytes;
+            if (!cuda_ok(cudaMemcpyAsync(dst + a, staging + (a - lo), b - a, cudaMemcpyDeviceToHost, nullptr), error,
+                         "device-to-host copy"))
+                return false;
+            written.emplace_back(a, b);
+            k = e + 1;
+        }
+        for (size_t i : direct) {
+            const Piece& pc = *placed[i].piece;
+            if (pc.device != device) continue;
+            if (!cuda_ok(cudaMemcpyAsync(dst + placed[i].at, static_cast<const uint8_t*>(pc.dev.base) + pc.from,
+                                         pc.bytes, cudaMemcpyDeviceToHost, nullptr),
+                         error, "running-state copy"))
+                return false;
+            written.emplace_back(placed[i].at, placed[i].at + pc.bytes);
+        }
+        if (!cuda_ok(cudaStreamSynchronize(nullptr), error, "synchronize") || !status_clean(device, error)) return false;
+    }
+    for (size_t i : direct) {   // sub-16-byte pieces of a device with nothing to gather
+        const Piece& pc = *placed[i].piece;
+        if (by_device.count(pc.device)) continue;
+        const DeviceScope on(pc.device);
+        if (!cuda_ok(cudaMemcpy(dst + placed[i].at, static_cast<const uint8_t*>(pc.dev.base) + pc.from, pc.bytes,
+                                cudaMemcpyDeviceToHost),
+                     error, "running-state copy"))
+            return false;
+        written.emplace_back(placed[i].at, placed[i].at + pc.bytes);
+    }
+    for (size_t i : host) {
+        const Piece& pc = *placed[i].piece;
+        std::memcpy(dst + placed[i].at, pc.host, pc.bytes);
+        written.emplace_back(placed[i].at, placed[i].at + pc.bytes);
+    }
+    std::sort(written.begin(), written.end());
+    uint64_t cursor = p.blob_pool_off;
+    for (const auto& [a, b] : written) {
+        if (a > cursor) std::memset(dst + cursor, 0, a - cursor);
+        cursor = std::max(cursor, b);
+    }
+    if (p.total_bytes > cursor) std::memset(dst + cursor, 0, p.total_bytes - cursor);
+
+    plan = p;
+    out.bytes = p.total_bytes;
+    out.payload_hash = opt.hash ? fnv1a64(dst, p.total_bytes) : 0;
+    out.blob_pool_bytes = p.blob_pool_bytes;
+    out.blobs = blobs.size();
+    return true;
+}
+
+bool conversation_wire_pack_device(const ConversationView& view, const SessionState& ss, const ModelGeometry& g,
+                                   const QsaState& draft, const WireIdentity& identity, uint8_t* dst,
+                                   uint64_t capacity, WirePlan& plan, WireEncoded& out, std::string& error,
+                                   const WireDeviceOptions& opt) {
+    return conversation_wire_pack_device(view, ss, {}, g, draft, identity, dst, capacity, plan, out, error, opt);
+}
+
+}  // namespace strata::core

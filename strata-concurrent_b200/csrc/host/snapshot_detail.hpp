@@ -29,6 +29,32 @@ std::array<const void*, 5> layer_sources(const QsaState& st);
 /// Stream `i` of a layer as the copy kernels address it (paged through page_table for the K/V streams).
 strata::kv::DeviceStream layer_stream(const QsaState& st, const LayerExtent& x, int i, const void* base);
 
+/// The 18-entry geometry key every image and payload carries.
+std::array<int64_t, 18> geometry_key(const ModelGeometry& g);
+
+/// Make `device` current for a scope (a negative device, or the current one, changes nothing).
+struct DeviceScope {
+    int previous = -1;
+    explicit DeviceScope(int device);
+    ~DeviceScope();
+    DeviceScope(const DeviceScope&) = delete;
+    DeviceScope& operator=(const DeviceScope&) = delete;
+};
+bool device_sync(std::string& error);
+
+size_t owned_count(const SessionState& ss);
+const QsaState& owned_layer(const SessionState& ss, size_t j);
+int64_t stage_count(const ConversationStageSet& s);
+/// The session can hold a `tokens`-long running state (sizes, pointers, indexer capacity); `z` gets the sizes.
+bool running_targets(const SessionState& ss, const ModelGeometry& g, size_t tokens, ConversationStateSizes& z,
+                     std::string& error);
+/// The main session plus the stages tile [0, n_layers) in order.
+bool stages_tile(const ConversationStageSet& stages, const SessionState& main_ss, const ModelGeometry& g,
+                 std::string& error);
+/// The live branch and every retained checkpoint are consistent prefixes of it.
+bool view_ok(const ConversationView& view, const SessionState& ss, const ConversationStageSet& stages,
+             const ModelGeometry& g, std::string& error);
+
 /// Queue one layer's save / restore into a batch (validation happens here, before anything is queued).
 bool enqueue_kv_save(ConversationKv& image, const QsaState& st, const ModelGeometry& g, int64_t upto, bool index,
                      strata::kv::Transfer& t, std::string& error, int64_t unchanged, size_t* reused_bytes);

@@ -59,6 +59,10 @@ void pieces_of(strata::core::ConversationBuffer& b, uint64_t from, uint64_t to, 
 
 }  // namespace
 
+bool transfer_staging(uint64_t bytes, uint8_t** out, std::string& error, const char* what) {
+    return staging_for(bytes, out, error, what);
+}
+
 uint64_t transfer_staging_bytes(int device) {
     std::lock_guard<std::mutex> lock(g_staging_mu);
     auto it = g_staging.find(device);

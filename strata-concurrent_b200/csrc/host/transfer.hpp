@@ -68,5 +68,8 @@ private:
 
 /// Bytes of the per-device staging image currently held (for tests and telemetry).
 uint64_t transfer_staging_bytes(int device);
+/// The current device's staging image (kept between calls, grown on demand), at least `bytes` long.  Shared by
+/// every batch on that device: one batch at a time per device.
+bool transfer_staging(uint64_t bytes, uint8_t** out, std::string& error, const char* what);
 
 }  // namespace strata::kv

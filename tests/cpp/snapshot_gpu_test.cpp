@@ -4,7 +4,9 @@
 // seed-random slots - a NON-identity page table - and parked with conversation_snapshot_save.  The parked image,
 // encoded with the SR4H codec, must hash to exactly the FNV-1a the reference's own save + encode produced from
 // its identity-layout pool (tests/golden/golden.json, passed on the command line).  The image is then mounted into
-// a second pool with different random slots and every byte is read back through that pool's table.
+// a second pool with different random slots and every byte is read back through that pool's table.  The
+// device-side pack must write the same payload straight from the permuted pool, into pinned host memory and into
+// device memory, and that payload must decode back to the parked image.
 //
 // Usage: snapshot_gpu_test <golden payload bytes> <golden payload fnv>      (exit 0 = pass)
 // The synthetic content comes from the test oracle's seeded generators (oracle/kv_oracle.c), the same calls
@@ -12,6 +14,7 @@
 #include "strata_kv.h"
 #include "strata_kv/conversation_snapshot.hpp"
 #include "strata_kv/conversation_wire.hpp"
+#include "strata_kv/conversation_wire_device.hpp"
 
 extern "C" {
 #include "kv_oracle.h"
@@ -288,6 +291,81 @@ int main(int argc, char** argv) {
     check_ok(conversation_wire_encode(img, sink, {geom_hash, pack_hash}, enc, err), err, "encoded");
     check(enc.bytes == golden_bytes, "the payload has the reference's length");
     check(enc.payload_hash == golden_hash, "the payload's FNV-1a is the reference's (every byte identical)");
+    t0 = std::chrono::steady_clock::now();
+    {
+        VectorWireSink again_sink(golden_bytes);
+        WireEncoded again_enc;
+        check_ok(conversation_wire_encode(img, again_sink, {geom_hash, pack_hash}, again_enc, err), err, "encoded again");
+    }
+    const double encode_ms = ms_since(t0);
+
+    // ---- the device-side pack: the same payload straight from the permuted pool, no host image in between
+    double pack_ms = 0, pack_hash_ms = 0, pack_dev_ms = 0;
+    {
+        WirePlan plan;
+        check_ok(conversation_wire_pack_plan(view, a.ss, g, a.draft, plan, err), err, "device pack planned");
+        check(plan.total_bytes == golden_bytes, "the planned payload has the reference's length");
+        uint8_t* pinned = nullptr;
+        cuda(cudaHostAlloc(reinterpret_cast<void**>(&pinned), plan.total_bytes, cudaHostAllocDefault), "pinned payload");
+        std::memset(pinned, 0xA5, plan.total_bytes);   // every byte has to be written by the pack
+        WirePlan used;
+        WireEncoded denc;
+        t0 = std::chrono::steady_clock::now();
+        check_ok(conversation_wire_pack_device(view, a.ss, g, a.draft, {geom_hash, pack_hash}, pinned, plan.total_bytes,
+                                               used, denc, err),
+                 err, "device pack into pinned host memory");
+        pack_hash_ms = ms_since(t0);
+        check(denc.bytes == golden_bytes, "the device-packed payload has the reference's length");
+        check(denc.payload_hash == golden_hash, "the device-packed payload's FNV-1a is the reference's");
+        check(std::memcmp(pinned, sink.data().data(), golden_bytes) == 0, "and it equals the host encoder's bytes");
+        check(used.total_bytes == plan.total_bytes && denc.blobs == plan.blobs, "the pack follows its plan");
+
+        std::memset(pinned, 0x5A, plan.total_bytes);
+        WireDeviceOptions no_hash;
+        no_hash.hash = false;
+        t0 = std::chrono::steady_clock::now();
+        check_ok(conversation_wire_pack_device(view, a.ss, g, a.draft, {geom_hash, pack_hash}, pinned, plan.total_bytes,
+                                               used, denc, err, no_hash),
+                 err, "device pack without the host hash pass");
+        pack_ms = ms_since(t0);
+        check(denc.payload_hash == 0, "no hash when none is asked for");
+        check(fnv1a64(pinned, golden_bytes) == golden_hash, "a second pack over other garbage writes the same bytes");
+
+        SavedConversation decoded;
+        WireDecoded info;
+        WireExpect expect;
+        expect.check_payload_hash = true;
+        expect.payload_hash = golden_hash;
+        check_ok(conversation_wire_decode(pinned, golden_bytes, decoded, info, expect, err), err,
+                 "the device-packed payload decodes");
+        check(decoded.kv.size() == img.kv.size(), "every layer decoded");
+        for (size_t j = 0; j < img.kv.size(); ++j)
+            check(decoded.kv[j].k == img.kv[j].k && decoded.kv[j].v == img.kv[j].v &&
+                      decoded.kv[j].pooled == img.kv[j].pooled,
+                  "decoded K/V and indexer rows equal the parked image");
+        check(decoded.live.gdn == img.live.gdn && decoded.live.tails == img.live.tails &&
+                  decoded.live.dead == img.live.dead && decoded.live.block_pos == img.live.block_pos,
+              "decoded running state equals the parked image");
+
+        uint8_t* on_device = nullptr;
+        cuda(cudaMalloc(&on_device, plan.total_bytes), "device payload");
+        cuda(cudaMemset(on_device, 0xA5, plan.total_bytes), "device payload garbage");
+        t0 = std::chrono::steady_clock::now();
+        check_ok(conversation_wire_pack_device(view, a.ss, g, a.draft, {geom_hash, pack_hash}, on_device,
+                                               plan.total_bytes, used, denc, err),
+                 err, "device pack into device memory");
+        pack_dev_ms = ms_since(t0);
+        std::vector<uint8_t> back(golden_bytes);
+        cuda(cudaMemcpy(back.data(), on_device, golden_bytes, cudaMemcpyDeviceToHost), "device payload read back");
+        check(back == sink.data(), "the device-resident payload equals the host encoder's bytes");
+
+        check(!conversation_wire_pack_device(view, a.ss, g, a.draft, {geom_hash, pack_hash}, pinned,
+                                             plan.total_bytes - 1, used, denc, err),
+              "a destination one byte short is refused");
+        check(err.find("needs") != std::string::npos, "and the refusal names the size");
+        cudaFree(on_device);
+        cudaFreeHost(pinned);
+    }
 
     // ---- mount into a pool with different random slots
     DeviceSession b(g, T, 4096, 23);
@@ -363,6 +441,9 @@ int main(int argc, char** argv) {
     }
     std::printf("park %.2f ms, mount %.2f ms for %.1f MB of K/V + state (%llu payload bytes)\n", park_ms, mount_ms,
                 (double) img.bytes() / 1e6, (unsigned long long) enc.bytes);
+    std::printf("host encode %.2f ms; device pack %.2f ms to pinned host (%.2f ms with the FNV pass), %.2f ms to "
+                "device memory\n",
+                encode_ms, pack_ms, pack_hash_ms, pack_dev_ms);
     std::printf("snapshot_gpu_test: %d checks passed\n", checks);
     return 0;
 }
