@@ -55,6 +55,9 @@ def parse():
     ap.add_argument("--seed", type=int, default=1)
     ap.add_argument("--pool-blocks", type=int, default=4096, help="slots per pool (the configs use 4,096)")
     ap.add_argument("--p2p", default="pull", choices=["pull", "push"], help="N > 1: which GPU runs the copy")
+    ap.add_argument("--scenario", default="pairs", choices=["pairs", "fanout"],
+                    help="N > 1: prefill/decode pairs (configs 3/5) or one prefill fanned out to N-1 decodes (config 4)")
+    ap.add_argument("--chunk-mb", type=int, default=32, help="fan-out chain: pipeline chunk size")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     return ap.parse_args()
@@ -225,35 +228,126 @@ def time_steps(torch, stream, fn, steps: int, warmup: int) -> tuple:
     return ev[0].elapsed_time(ev[steps]), per
 
 
+def pcie_probe(torch, nbytes: int = 1 << 30, reps: int = 5) -> dict:
+    """The box's pinned-host copy rates (the park/resume roofline): one direction at a time, then both at once
+    on two streams.  Median of `reps`, CUDA events."""
+    host_a = torch.empty(nbytes, dtype=torch.uint8, pin_memory=True)
+    host_b = torch.empty(nbytes, dtype=torch.uint8, pin_memory=True)
+    dev_a = torch.empty(nbytes, dtype=torch.uint8, device="cuda")
+    dev_b = torch.empty(nbytes, dtype=torch.uint8, device="cuda")
+    s1, s2 = torch.cuda.Stream(), torch.cuda.Stream()
+
+    def timed(fn):
+        out = []
+        for _ in range(reps + 1):
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(s1)
+            s2.wait_event(e0)
+            fn()
+            done = torch.cuda.Event()
+            done.record(s2)
+            s1.wait_event(done)
+            e1.record(s1)
+            torch.cuda.synchronize()
+            out.append(e0.elapsed_time(e1))
+        return float(np.median(out[1:]))
+
+    def d2h():
+        with torch.cuda.stream(s1):
+            host_a.copy_(dev_a, non_blocking=True)
+
+    def h2d():
+        with torch.cuda.stream(s1):
+            dev_b.copy_(host_b, non_blocking=True)
+
+    def both():
+        with torch.cuda.stream(s1):
+            host_a.copy_(dev_a, non_blocking=True)
+        with torch.cuda.stream(s2):
+            dev_b.copy_(host_b, non_blocking=True)
+
+    t_d2h, t_h2d, t_both = timed(d2h), timed(h2d), timed(both)
+    gb = nbytes / 1e9
+    return {"d2h_gbs": round(gb / (t_d2h / 1e3), 2), "h2d_gbs": round(gb / (t_h2d / 1e3), 2),
+            "both_directions_gbs": round(2 * gb / (t_both / 1e3), 2),
+            "probe": f"{nbytes >> 20} MiB pinned <-> device copies, median of {reps}"}
+
+
+RELAY_CHUNK_BYTES = 32 << 20
+
+
+def relay_pieces(park_segs: list, resume_segs: list) -> list:
+    """A pipelined host relay's chunks: every park segment and its resume twin cut into the same pieces of at most
+    RELAY_CHUNK_BYTES, as (park piece, resume piece) pairs in order."""
+    out = []
+    for p, r in zip(park_segs, resume_segs):
+        out += list(zip(skv.split_segment(p, RELAY_CHUNK_BYTES), skv.split_segment(r, RELAY_CHUNK_BYTES)))
+    return out
+
+
 def e2e_park_resume(torch, kg, src: SeqOnGpu, dst: SeqOnGpu, steps: int, warmup: int) -> dict:
-    """Host-mediated handoff through the C ABI: park to pinned host, resume into another table."""
+    """Host-mediated handoff through the C ABI: park to pinned host, resume into another table.
+
+    staged / direct: one skv_park then one skv_resume of the whole sequence.
+    relay: the same calls chunk by chunk on two streams - skv_park of chunk c+1 (device -> host) runs while
+           skv_resume of chunk c (host -> device) runs, so both PCIe directions are busy at once."""
     off = skv.image_offsets(kg, src.tokens, kg.n_qsa)
     host = skv.HostBuffer(off["total"])
     staging = torch.empty(off["total"] + 256 * 64, dtype=torch.uint8, device="cuda")
+    staging_b = torch.empty(off["total"] + 256 * 64, dtype=torch.uint8, device="cuda")
     stream = torch.cuda.current_stream()
+    side = torch.cuda.Stream()
+    park_segs = skv.pack_segments(src.ps, host.ptr)
+    resume_segs = skv.unpack_segments(host.ptr, dst.ps)
+    chunks = relay_pieces(park_segs, resume_segs)
+    chunk_off = []
+    at = 0
+    for pp, _ in chunks:
+        chunk_off.append(at)
+        at += (pp.bytes + 255) & ~255
+    parked = [torch.cuda.Event() for _ in chunks]
+    resumed = torch.cuda.Event()
     best = None
-    for mode, name in ((skv.PARK_STAGED, "staged"), (skv.PARK_DIRECT, "direct")):
-        def step():
-            skv.park(skv.pack_segments(src.ps, host.ptr), mode, staging, staging.numel(), stream)
-            skv.resume(skv.unpack_segments(host.ptr, dst.ps), mode, staging, staging.numel(), stream)
+    parity, modes = {}, {}
+    for mode, name in ((skv.PARK_STAGED, "staged"), (skv.PARK_DIRECT, "direct"), (skv.PARK_STAGED, "relay")):
+        if name == "relay":
+            def step():
+                for k, (pp, rp) in enumerate(chunks):
+                    a = staging.data_ptr() + chunk_off[k]
+                    skv.park([pp], mode, a, staging.numel() - chunk_off[k], stream)
+                    parked[k].record(stream)
+                    side.wait_event(parked[k])
+                    b = staging_b.data_ptr() + chunk_off[k]
+                    skv.resume([rp], mode, b, staging_b.numel() - chunk_off[k], side)
+                resumed.record(side)
+                stream.wait_event(resumed)
+        else:
+            def step():
+                skv.park(park_segs, mode, staging, staging.numel(), stream)
+                skv.resume(resume_segs, mode, staging, staging.numel(), stream)
+        dst.pool_mem.zero_()
+        dst.gdn.zero_()
+        dst.ids.zero_()
         total, per = time_steps(torch, stream, step, steps, warmup)
+        parity[name] = (bool(torch.equal(dst.logical(torch), src.logical(torch))) and bool(torch.equal(dst.gdn, src.gdn))
+                        and bool(torch.equal(dst.ids, src.ids)))
         b = kg.metric_bytes(src.tokens)
         res = {"mode": name, "value": b * steps / (total / 1e3) / 1e9, "ms_per_step": total / steps,
                "p50_ms": percentiles(per)[0], "p99_ms": percentiles(per)[1],
-               # park and resume run one after the other, so each direction is busy half the step
-               "pcie_gbs_while_active": 2 * b * steps / (total / 1e3) / 1e9}
+               # bytes over PCIe in both directions together (B down + B up per step) per second
+               "pcie_gbs_both_directions": 2 * b * steps / (total / 1e3) / 1e9}
+        modes[name] = round(res["value"], 3)
         if best is None or res["value"] > best["value"]:
             best = res
-        best.setdefault("modes", {})[name] = round(res["value"], 3)
-    # parity of the last resume
-    ok = bool(torch.equal(dst.logical(torch), src.logical(torch))) and bool(torch.equal(dst.gdn, src.gdn))
+    ok = all(parity.values())
     host.close()
     out = {"value": round(best["value"], 3), "unit": UNIT, "h2d_bytes_per_step": kg.metric_bytes(src.tokens),
            "d2h_bytes_per_step": kg.metric_bytes(src.tokens), "mode": best["mode"],
            "p50_ms": round(best["p50_ms"], 3), "p99_ms": round(best["p99_ms"], 3),
-           "pcie_gbs_while_active": round(best["pcie_gbs_while_active"], 3),
-           "modes_gbs": best.get("modes", {}), "api": "skv_park + skv_resume (C ABI), pinned host image",
-           "parity": ok}
+           "pcie_gbs_both_directions": round(best["pcie_gbs_both_directions"], 3),
+           "modes_gbs": modes, "api": "skv_park + skv_resume (C ABI), pinned host image",
+           "parity": ok, "parity_by_mode": parity}
     return out
 
 
@@ -399,7 +493,15 @@ def run_single(args, torch) -> None:
                          "algorithmic_bytes_per_launch": 2 * b}}
     line["clocks"] = clk.summary()
     if not args.no_e2e:
-        line["e2e"] = e2e_park_resume(torch, kg, src, dst, max(3, args.steps // 4), 2)
+        e2e = e2e_park_resume(torch, kg, src, dst, max(3, args.steps // 4), 2)
+        pcie = pcie_probe(torch)
+        e2e["pcie_peak"] = pcie
+        # the relay keeps both directions busy, so its bound is the two-direction probe; a serial park + resume
+        # is bound by one direction at a time
+        bound = pcie["both_directions_gbs"] if e2e["mode"] == "relay" else 2 / (1 / pcie["d2h_gbs"] + 1 / pcie["h2d_gbs"])
+        e2e["pcie_frac"] = round(e2e["pcie_gbs_both_directions"] / bound, 4) if e2e["mode"] == "relay" else \
+            round(e2e["value"] * 2 / bound, 4)
+        line["e2e"] = e2e
     if not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(t)
     print(json.dumps(line))
@@ -415,11 +517,14 @@ def pair_role(rank: int, world: int) -> tuple:
     return role, peer, rank < 2 * pairs
 
 
+FLAGS = 128   # 8-byte flag words per state arena (chunk flags of a pipelined fan-out, completion flags)
+
+
 def state_layout(kg: skv.KvGeometry, tokens: int) -> dict:
-    """The decode GPU's per-sequence state arena: GDN rows | ids (16-byte rounded) | completion flag."""
+    """The decode GPU's per-sequence state arena: GDN rows | ids (16-byte rounded) | FLAGS flag words."""
     ids_off = kg.gdn_bytes
     flag_off = (ids_off + ((4 * tokens + 15) // 16) * 16 + 255) // 256 * 256
-    total = (flag_off + 256 + 1023) // 1024 * 1024
+    total = (flag_off + 8 * FLAGS + 1023) // 1024 * 1024
     return {"ids": ids_off, "flag": flag_off, "bytes": total}
 
 
@@ -565,6 +670,213 @@ def run_pairs(args, torch) -> None:
     dist.destroy_process_group()
 
 
+# ------------------------------------------------------------------------------------------------ fan-out
+
+def run_fanout(args, torch) -> None:
+    """Config 4: rank 0 (prefill) holds one sequence; ranks 1..N-1 (decode) each receive the whole cache into
+    their own pool at independent random slots.  Three ways, each timed over the same K steps:
+
+      p2p    every receiver pulls the whole sequence from rank 0's pool at once (the source's NVLink egress
+             carries the cache N-1 times);
+      nccl   rank 0 packs the sequence into a contiguous image (gather kernel), ncclBroadcast sends it, each
+             receiver scatters it into its pool (the reference-style collective path);
+      chain  receiver k pulls chunk c of the cache from receiver k-1's pool as soon as k-1 signals it landed, so
+             every NVLink hop carries the cache once and the hops overlap chunk by chunk.
+
+    value = receivers x B(T) x K / max-over-ranks timed region (fan-out counts every receiver's bytes)."""
+    import torch.distributed as dist
+    from datetime import timedelta
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    local = int(os.environ.get("LOCAL_RANK", rank))
+    torch.cuda.set_device(local)
+    dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+    kg = skv.KvGeometry()
+    t = args.tokens
+    receivers = world - 1
+    lay = state_layout(kg, t)
+    stream = torch.cuda.current_stream()
+    sp = stream.cuda_stream
+    L = skv.lib()
+    n_blocks = max(args.pool_blocks, kg.n_qsa * kg.blocks(t))
+    seq = SeqOnGpu(torch, kg, t, n_blocks, seed=args.seed + 1000 * rank, fill=rank == 0, ipc=True)
+    mine = {"pool": skv.ipc_export(seq.pool.base), "state": skv.ipc_export(seq.state.base), "tables": seq.host_tables}
+    torch.cuda.synchronize()
+    handles = [None] * world
+    dist.all_gather_object(handles, mine)
+    maps = {}                    # rank -> (pool base, state base) mapped here
+
+    def peer(r):
+        if r not in maps:
+            maps[r] = (skv.ipc_import(local, handles[r]["pool"]), skv.ipc_import(local, handles[r]["state"]))
+        return maps[r]
+
+    def peer_seq(r):
+        pool, state = peer(r)
+        tables = torch.from_numpy(handles[r]["tables"].reshape(-1).copy()).cuda()
+        return skv.PooledSequence(kg, skv.Pool(local, n_blocks, kg.block_bytes, memory=pool), t, kg.n_qsa, None,
+                                  tables, state, state + lay["ids"]), tables
+
+    flag = lambda base, i: base + lay["flag"] + 8 * i            # noqa: E731
+    DONE = FLAGS - 1 - receivers                                  # rank 0's flags DONE+1 .. DONE+receivers
+    wait_ns = 5_000_000_000
+    off = skv.image_offsets(kg, t, kg.n_qsa)
+    image = torch.empty(off["total"], dtype=torch.uint8, device="cuda")
+    chunk_bytes = args.chunk_mb << 20
+    keep = []                    # tables of mapped peers stay alive
+    results = {}
+    counter = [0]
+
+    def timed(step):
+        dist.barrier()
+        for _ in range(args.warmup):
+            step()
+        torch.cuda.synchronize()
+        dist.barrier()
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
+        ev[0].record(stream)
+        for i in range(args.steps):
+            step()
+            ev[i + 1].record(stream)
+        torch.cuda.synchronize()
+        dist.barrier()
+        per = torch.tensor([ev[i].elapsed_time(ev[i + 1]) for i in range(args.steps)], device="cuda")
+        tot = torch.tensor([ev[0].elapsed_time(ev[args.steps])], device="cuda")
+        dist.all_reduce(tot, op=dist.ReduceOp.MAX)
+        dist.all_reduce(per, op=dist.ReduceOp.MAX)
+        return float(tot.item()), per.cpu().numpy()
+
+    def parity():
+        """Every receiver's cache, packed through its own table, equals the source's packed cache."""
+        mine_img = seq.packed(torch)
+        ref = mine_img if rank == 0 else torch.empty_like(mine_img)
+        dist.broadcast(ref, 0)
+        ok = torch.tensor([float(bool(torch.equal(ref, mine_img)))], device="cuda")
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+        return bool(ok.item() == 1.0)
+
+    def clear_receiver():
+        if rank:
+            zero = torch.zeros(1 << 28, dtype=torch.uint8, device="cuda")
+            total = n_blocks * kg.block_bytes
+            for at in range(0, total, zero.numel()):
+                n = min(zero.numel(), total - at)
+                skv.copy([skv.segment(zero, seq.pool.base + at, n)], skv.COPY_VEC)
+            skv.copy([skv.segment(zero, seq.gdn, kg.gdn_bytes)], skv.COPY_VEC)
+            torch.cuda.synchronize()
+        dist.barrier()
+
+    # ---- p2p: every receiver pulls from rank 0 at once
+    if rank == 0:
+        rflags = [peer(r)[1] for r in range(1, world)]
+
+        def step():
+            counter[0] += 1
+            for r, st in enumerate(rflags):
+                skv.check(L.skv_signal(flag(st, 0), counter[0], sp))                 # READY
+            for r in range(receivers):
+                skv.check(L.skv_wait_flag(flag(seq.state.base, DONE + 1 + r), counter[0], wait_ns, sp))
+    else:
+        src, tab = peer_seq(0)
+        keep.append(tab)
+        segs = skv.kv_segments_pool_to_pool(src, seq.ps) + skv.state_segments(src, seq.gdn, seq.ids)
+        arr = (skv.Segment * len(segs))(*segs)
+        done0 = flag(peer(0)[1], DONE + rank)
+
+        def step():
+            counter[0] += 1
+            skv.check(L.skv_wait_flag(flag(seq.state.base, 0), counter[0], wait_ns, sp))
+            skv.check(L.skv_copy(arr, len(segs), skv.COPY_TMA, sp))
+            skv.check(L.skv_signal(done0, counter[0], sp))
+    clear_receiver()
+    skv.clear_status(local)
+    results["p2p"] = timed(step) + (parity(),)
+
+    # ---- nccl: pack, broadcast, scatter
+    pack = (skv.Segment * len(s0 := skv.pack_segments(seq.ps, image)))(*s0)
+    unpack = (skv.Segment * len(s1 := skv.unpack_segments(image, seq.ps)))(*s1)
+
+    def step():
+        if rank == 0:
+            skv.check(L.skv_copy(pack, len(s0), skv.COPY_TMA, sp))
+        dist.broadcast(image, 0)
+        if rank:
+            skv.check(L.skv_copy(unpack, len(s1), skv.COPY_TMA, sp))
+    clear_receiver()
+    results["nccl"] = timed(step) + (parity(),)
+
+    # ---- chain: receiver k pulls chunk c from receiver k-1 once k-1 has it
+    counter[0] = 10 ** 6          # flag values keep growing across methods
+    if rank == 0:
+        first = flag(peer(1)[1], 0)
+
+        def step():
+            counter[0] += 1
+            skv.check(L.skv_signal(first, counter[0], sp))                           # READY to receiver 1
+            skv.check(L.skv_wait_flag(flag(seq.state.base, DONE + receivers), counter[0], wait_ns, sp))
+        n_chunks = 0
+    else:
+        up, tab = peer_seq(rank - 1)
+        keep.append(tab)
+        whole = skv.kv_segments_pool_to_pool(up, seq.ps) + skv.state_segments(up, seq.gdn, seq.ids)
+        pieces = [p for w in whole for p in skv.split_segment(w, chunk_bytes)]
+        n_chunks = len(pieces)
+        if n_chunks > FLAGS - 1 - receivers:
+            raise SystemExit(f"--chunk-mb {args.chunk_mb} gives {n_chunks} chunks; at most {FLAGS - 1 - receivers}")
+        # one chained launch per group of at most SKV_COPY_MAX_SEGMENTS chunks: in-kernel waits on this GPU's
+        # chunk flags (set by the previous receiver), in-kernel release stores to the next receiver's flags
+        groups = [(g0, (skv.Segment * len(pieces[g0:g0 + skv.MAX_SEGMENTS]))(*pieces[g0:g0 + skv.MAX_SEGMENTS]))
+                  for g0 in range(0, n_chunks, skv.MAX_SEGMENTS)]
+        down = peer(rank + 1)[1] if rank < receivers else None
+        done0 = flag(peer(0)[1], DONE + receivers)
+
+        def step():
+            counter[0] += 1
+            if rank == 1:
+                skv.check(L.skv_wait_flag(flag(seq.state.base, 0), counter[0], wait_ns, sp))   # READY
+            for g0, arr in groups:
+                wait = None if rank == 1 else flag(seq.state.base, g0)
+                signal = flag(down, g0) if down else None
+                skv.check(L.skv_copy_chained(arr, len(arr), wait, signal, counter[0], wait_ns, sp))
+            if not down:
+                skv.check(L.skv_signal(done0, counter[0], sp))
+    clear_receiver()
+    results["chain"] = timed(step) + (parity(),)
+    status = torch.tensor([float(skv.query_status(local) != 0)], device="cuda")
+    dist.all_reduce(status, op=dist.ReduceOp.MAX)
+
+    b = kg.metric_bytes(t)
+    if rank == 0:
+        methods = {}
+        for name, (tot, per, ok) in results.items():
+            methods[name] = {"value": round(receivers * b * args.steps / (tot / 1e3) / 1e9, 3),
+                             "ms_per_step": round(tot / args.steps, 4),
+                             "p50_ms": round(float(np.percentile(per, 50)), 4),
+                             "p99_ms": round(float(np.percentile(per, 99)), 4),
+                             "per_receiver_gbs": round(b * args.steps / (tot / 1e3) / 1e9, 3), "parity": ok}
+        best = max(methods, key=lambda k: methods[k]["value"])
+        m = methods[best]
+        line = {"metric": METRIC, "value": m["value"], "unit": UNIT, "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": m["ms_per_step"], "p50_ms": m["p50_ms"], "p99_ms": m["p99_ms"],
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u8", "data": "synthetic",
+                "config": {"workload": f"config 4: 1 prefill GPU fans one {t}-token cache out to {receivers} decode "
+                                       f"GPUs (independent random tables); best of p2p / nccl broadcast / chained pull",
+                           "tokens": t, "receivers": receivers, "method": best, "chunk_mb": args.chunk_mb,
+                           "l2": "inputs larger than L2", "parallelism": f"1 -> {receivers} fan-out"},
+                "methods": methods, "parity": all(v["parity"] for v in methods.values()) and status.item() == 0,
+                "roofline": {"bound": "nvlink", "achieved": m["per_receiver_gbs"], "peak": NVLINK_PEER_COPY_GBS,
+                             "unit": "GB/s", "frac": round(m["per_receiver_gbs"] / NVLINK_PEER_COPY_GBS, 4),
+                             "peak_kind": "measured peer copy per direction; each receiver's ingress",
+                             "traffic": None, "kernel": "copy_tma_kernel"}}
+        print(json.dumps(line))
+    torch.cuda.synchronize()
+    dist.barrier()
+    for pool, state in maps.values():
+        skv.ipc_close(pool)
+        skv.ipc_close(state)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
 def main() -> None:
     args = parse()
     if args.impl == "reference":
@@ -572,7 +884,9 @@ def main() -> None:
         return
     import torch
     world = int(os.environ.get("WORLD_SIZE", "1"))
-    if world > 1:
+    if world > 1 and args.scenario == "fanout":
+        run_fanout(args, torch)
+    elif world > 1:
         run_pairs(args, torch)
     else:
         run_single(args, torch)

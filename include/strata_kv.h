@@ -168,6 +168,17 @@ SKV_API int skv_host_free(void* p);
 SKV_API int skv_park(const skv_segment* segs, int n_segs, int mode, void* staging, uint64_t staging_bytes, void* stream);
 SKV_API int skv_resume(const skv_segment* segs, int n_segs, int mode, void* staging, uint64_t staging_bytes, void* stream);
 
+/* Chained copy (no reference counterpart: the pipelined relay of a one-to-many handoff).  Like skv_copy with
+ * the TMA engine, but segment c is chunk c of a pipeline: no byte of chunk c is read before
+ * wait_flags[c] >= value (this device's memory; bounded by timeout_ns of device time, 0 = 2 s), and once every
+ * byte of chunk c has landed, value is stored to signal_flags[c] (any device's memory, e.g. the next GPU's
+ * flags through CUDA IPC) with system-scope release semantics - while later chunks are still moving.  Either
+ * flag array may be NULL.  Every chunk must be non-empty.  A wait that runs out sets SKV_STATUS_WAIT_TIMEOUT,
+ * stops new reads, and leaves the unfinished chunks unsignalled.  One chained copy in flight per device (the
+ * per-chunk counters are per device). */
+SKV_API int skv_copy_chained(const skv_segment* segs, int n_segs, const uint64_t* wait_flags, uint64_t* signal_flags,
+                             uint64_t value, uint64_t timeout_ns, void* stream);
+
 /* ------------------------------------------------------------------ peer-to-peer handoff
  * The reference has no P2P path at all (its multi-GPU split stages through pinned RAM, docs/MULTI_GPU.md:9-12).
  * skv_copy with destinations in a peer's pool is the P2P scatter; these make the peer reachable and give

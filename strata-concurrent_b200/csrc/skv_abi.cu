@@ -314,6 +314,29 @@ int skv_copy(const skv_segment* segs, int n_segs, int engine, void* stream) {
     return launch_copy(plan, tiles, engine, *ctx, static_cast<cudaStream_t>(stream));
 }
 
+int skv_copy_chained(const skv_segment* segs, int n_segs, const uint64_t* wait_flags, uint64_t* signal_flags,
+                     uint64_t value, uint64_t timeout_ns, void* stream) {
+    DeviceCtx* ctx = current_ctx();
+    if (!ctx) return SKV_ECUDA;
+    if (n_segs < 1 || n_segs > SKV_COPY_MAX_SEGMENTS || !segs)
+        return fail(SKV_EINVAL, "skv_copy_chained: chunk count must be in [1, SKV_COPY_MAX_SEGMENTS]");
+    for (int i = 0; i < n_segs; ++i)
+        if (segs[i].bytes == 0) return fail(SKV_EINVAL, "skv_copy_chained: every chunk must move at least one byte");
+    if ((reinterpret_cast<uintptr_t>(wait_flags) | reinterpret_cast<uintptr_t>(signal_flags)) & 7u)
+        return fail(SKV_EINVAL, "skv_copy_chained: flags must be 8-byte aligned");
+    CopyPlan plan;
+    uint64_t tiles = 0;
+    if (const int rc = build_plan(segs, n_segs, SKV_COPY_TMA, plan, tiles)) return rc;
+    if (!ctx->chain_landed) {
+        const cudaError_t e = cudaMalloc(&ctx->chain_landed, kChainScratchBytes);
+        if (e != cudaSuccess) return cuda_fail(e, "skv_copy_chained: counters");
+    }
+    plan.status = ctx->status;
+    auto* next_tile = reinterpret_cast<unsigned long long*>(ctx->chain_landed + SKV_COPY_MAX_SEGMENTS);
+    ChainArgs chain{wait_flags, signal_flags, ctx->chain_landed, next_tile, value, timeout_ns ? timeout_ns : 2000000000ull};
+    return launch_copy_chained(plan, tiles, chain, *ctx, static_cast<cudaStream_t>(stream));
+}
+
 int skv_set_copy_tuning(int tma_stages, uint32_t tma_tile_bytes, int tma_ctas_per_sm, int vec_ctas_per_sm) {
     if (tma_stages < 2 || tma_stages > kTmaMaxStages || tma_tile_bytes < kTmaMinTileBytes ||
         tma_tile_bytes > kTmaMaxTileBytes || tma_tile_bytes % 1024 || tma_ctas_per_sm < 1 || tma_ctas_per_sm > 8 ||

@@ -252,6 +252,197 @@ __global__ void __launch_bounds__(32) copy_tma_kernel(const __grid_constant__ Co
     bulk_wait_all();
 }
 
+// ---------------------------------------------------------------- chained TMA engine
+//
+// skv_copy_chained: the TMA engine with segment c as chunk c of a pipeline.  CTAs CLAIM tiles (two consecutive
+// at a time) from a global counter (not a static stride), so tiles are moved close to their global order and a chunk completes soon after
+// its last tile is claimed - a static stride lets fast and slow CTAs drift apart over a long copy, and a chunk is
+// only as done as its slowest CTA.  Before loading a tile of a chunk it has not seen released, a CTA checks
+// wait_flags[c] >= value; if it is not yet set, the CTA first stores every tile it has loaded, then waits (lane
+// 0, relaxed polls with back-off, bounded), then acquires.  When a CTA's next tile lies in a later chunk it waits
+// for its bulk stores to land and adds its count for the chunk to landed[c] (gpu-scope release/acquire); the CTA
+// that completes the count stores value to signal_flags[c] with release semantics at system scope, so a peer
+// GPU that acquires that flag reads every byte of chunk c.  A wait that runs out stops new loads (status
+// WAIT_TIMEOUT); loaded tiles are still stored, and a chunk is signalled only if every one of its tiles landed.
+
+/// Lane 0 reads `flag` once (relaxed, system scope); the whole warp gets `flag >= value`.
+__device__ __forceinline__ bool warp_flag_set(const uint64_t* flag, uint64_t value, int lane) {
+    int ok = 0;
+    if (lane == 0) {
+        uint64_t v;
+        asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(flag) : "memory");
+        ok = v >= value;
+    }
+    return __shfl_sync(0xffffffffu, ok, 0) != 0;
+}
+
+/// Lane 0 polls `flag` >= value for at most timeout_ns with relaxed loads and a growing back-off (every CTA of the
+/// grid may be polling the same word).  Returns the verdict to the whole warp.
+__device__ __forceinline__ bool warp_wait_flag(const uint64_t* flag, uint64_t value, uint64_t timeout_ns, int lane) {
+    int ok = 1;
+    if (lane == 0) {
+        const uint64_t t0 = global_timer_ns();
+        uint32_t pause = 32;
+        for (;;) {
+            uint64_t v;
+            asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(flag) : "memory");
+            if (v >= value) break;
+            if (global_timer_ns() - t0 > timeout_ns) {
+                ok = 0;
+                break;
+            }
+            __nanosleep(pause);
+            pause = min(pause * 2u, 1024u);
+        }
+    }
+    return __shfl_sync(0xffffffffu, ok, 0) != 0;
+}
+
+/// After a flag was seen set: an acquire read of it (lane 0; the flag only grows, so this read sees it set too),
+/// then every lane orders its later bulk (async-proxy) loads after that acquire.
+__device__ __forceinline__ uint64_t ld_acquire_sys(const uint64_t* flag) {
+    uint64_t v;
+    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(flag) : "memory");
+    return v;
+}
+__device__ __forceinline__ void warp_acquire_flag(const uint64_t* flag, int lane) {
+    if (lane == 0) (void) ld_acquire_sys(flag);
+    __syncwarp();
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
+constexpr uint32_t kChainClaimBatch = 2;   // consecutive tiles per claim: fewer atomics, chunks still land in order
+
+__global__ void __launch_bounds__(32) copy_tma_chain_kernel(const __grid_constant__ CopyPlan plan, uint64_t total_tiles,
+                                                            const ChainArgs chain) {
+    extern __shared__ __align__(1024) uint8_t smem[];
+    const int stages = plan.tma_stages;
+    const uint32_t tile = plan.tma_tile;
+    uint8_t* ring = smem;
+    StageStash* stash = reinterpret_cast<StageStash*>(smem + (size_t) stages * tile);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(stash + stages);
+    uint64_t* held = bars + stages;   // the global tile index each stage holds
+    const int lane = (int) threadIdx.x;
+    const unsigned full = 0xffffffffu;
+    constexpr uint64_t kNone = ~0ull;
+
+    if (lane == 0)
+        for (int s = 0; s < stages; ++s) mbar_init(&bars[s], 1);
+    fence_proxy_async_smem();
+    __syncwarp();
+
+    uint64_t pending = kNone;   // claimed, not yet loaded
+    bool exhausted = false;     // the counter ran past the last tile
+    uint64_t batch_next = 0, batch_end = 0;   // the rest of the last claimed batch
+    auto claim = [&]() {        // warp-uniform, never blocks
+        if (pending != kNone || exhausted) return;
+        if (batch_next == batch_end) {
+            unsigned long long t = 0;
+            if (lane == 0) t = atomicAdd(chain.next_tile, (unsigned long long) kChainClaimBatch);
+            t = __shfl_sync(full, t, 0);
+            if (t >= total_tiles) {
+                exhausted = true;
+                return;
+            }
+            batch_next = t;
+            batch_end = min((uint64_t) t + kChainClaimBatch, total_tiles);
+        }
+        pending = batch_next++;
+    };
+    int cleared = -1;      // the last chunk whose upstream flag this CTA has acquired
+    bool stop = false;     // a flag wait ran out: no new loads
+    uint64_t issued = 0;   // tiles this CTA has loaded ...
+    uint64_t k = 0;        // ... and stored (positions in its own order; stage = position % stages)
+    // Load while the ring has room.  The stage a load reuses held the tile at position issued - stages, already
+    // stored; its bulk store has finished reading shared memory once at most the newest group is pending.
+    auto fill = [&]() {
+        while (!stop && issued < k + (uint64_t) stages - (k ? 1u : 0u)) {
+            claim();
+            if (pending == kNone) return;
+            if (chain.wait_flags) {
+                const int c = locate(plan, pending);
+                if (c > cleared) {
+                    const uint64_t* f = chain.wait_flags + c;
+                    if (!warp_flag_set(f, chain.value, lane)) {
+                        if (issued > k) return;   // not released yet: store what is loaded first
+                        if (!warp_wait_flag(f, chain.value, chain.timeout_ns, lane)) {
+                            if (lane == 0) atomicOr(plan.status, SKV_STATUS_WAIT_TIMEOUT);
+                            stop = true;
+                            return;
+                        }
+                    }
+                    warp_acquire_flag(f, lane);
+                    cleared = c;
+                }
+            }
+            if (issued >= (uint64_t) stages) bulk_wait_read_1();
+            const int st = (int) (issued % stages);
+            if (lane == 0) held[st] = pending;
+            __syncwarp();
+            tma_issue_load(plan, pending, ring + (size_t) st * tile, &bars[st], stash[st], lane);
+            pending = kNone;
+            ++issued;
+        }
+    };
+
+    fill();
+    uint32_t count = 0;   // tiles of the current chunk this CTA stored and has not yet reported
+    bool timed_out = false;
+    while (k < issued) {
+        const int st = (int) (k % stages);
+        const uint32_t phase = (uint32_t) ((k / stages) & 1u);
+        if (!__all_sync(full, mbar_wait_bounded(&bars[st], phase))) {
+            timed_out = true;
+            break;
+        }
+        fence_proxy_async_smem();
+        const uint32_t len = stash[st].store_len[lane];
+        if (len) bulk_store(stash[st].store_addr[lane], ring + (size_t) st * tile + stash[st].smem_off[lane], len);
+        bulk_commit();
+        const uint64_t t = held[st];
+        ++k;
+        if (chain.signal_flags) {
+            const int c = locate(plan, t);
+            ++count;
+            // the next tile this CTA will store: already loaded, else the next claim (claiming never blocks)
+            uint64_t next = kNone;
+            if (k < issued) {
+                next = held[k % stages];
+            } else if (!stop) {
+                claim();
+                next = pending;
+            }
+            if (next == kNone || next >= plan.tile_end[c]) {   // leaving chunk c: report it
+                bulk_wait_all();   // this CTA's bulk stores have landed
+                asm volatile("fence.proxy.async.global;" ::: "memory");
+                __syncwarp();
+                if (lane == 0) {
+                    // gpu-scope release/acquire on the counter gathers every CTA's stores into the last reporter's
+                    // view; its system-scope release store then publishes them (release is cumulative)
+                    const uint64_t n_c = plan.tile_end[c] - (c ? plan.tile_end[c - 1] : 0);
+                    uint32_t before;
+                    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;"
+                                 : "=r"(before)
+                                 : "l"(chain.landed + c), "r"(count)
+                                 : "memory");
+                    if ((uint64_t) before + count == n_c)
+                        asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(chain.signal_flags + c), "l"(chain.value)
+                                     : "memory");
+                }
+                __syncwarp();
+                count = 0;
+            }
+        }
+        fill();
+    }
+    if (timed_out) {
+        if (lane == 0) atomicOr(plan.status, SKV_STATUS_WAIT_TIMEOUT);
+        for (uint64_t j = k; j < issued; ++j)
+            (void) mbar_wait_bounded(&bars[j % stages], (uint32_t) ((j / stages) & 1u));
+    }
+    bulk_wait_all();
+}
+
 // ---------------------------------------------------------------- 16-byte vector engine
 
 constexpr int kVecUnroll = 4;
@@ -363,6 +554,25 @@ int launch_copy(const CopyPlan& plan, uint64_t total_tiles, int engine, DeviceCt
     }
     const cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? SKV_OK : cuda_fail(e, "copy kernel launch");
+}
+
+int launch_copy_chained(const CopyPlan& plan, uint64_t total_tiles, const ChainArgs& chain, DeviceCtx& ctx,
+                        cudaStream_t stream) {
+    if (total_tiles == 0) return SKV_OK;
+    const Tuning tu = tuning();
+    const size_t smem = tma_smem_bytes(plan.tma_stages, plan.tma_tile) + 8 * (size_t) plan.tma_stages;   // + held[]
+    if (ctx.tma_chain_smem_configured < smem) {
+        const cudaError_t e =
+            cudaFuncSetAttribute(copy_tma_chain_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(copy_tma_chain_kernel)");
+        ctx.tma_chain_smem_configured = smem;
+    }
+    cudaError_t e = cudaMemsetAsync(chain.landed, 0, kChainScratchBytes, stream);   // landed[] and next_tile
+    if (e != cudaSuccess) return cuda_fail(e, "chained copy: counter reset");
+    const unsigned grid = (unsigned) std::min<uint64_t>(total_tiles, (uint64_t) ctx.sms * tu.tma_ctas_per_sm);
+    copy_tma_chain_kernel<<<grid, 32, smem, stream>>>(plan, total_tiles, chain);
+    e = cudaGetLastError();
+    return e == cudaSuccess ? SKV_OK : cuda_fail(e, "chained copy kernel launch");
 }
 
 int launch_signal(uint64_t* flag, uint64_t value, cudaStream_t stream) {

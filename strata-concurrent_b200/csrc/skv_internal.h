@@ -64,6 +64,22 @@ struct DeviceCtx {
     int sms = 0;
     uint32_t* status = nullptr;
     size_t tma_smem_configured = 0;   // the copy_tma_kernel dynamic-smem limit set on this device so far
+    size_t tma_chain_smem_configured = 0;
+    uint32_t* chain_landed = nullptr; // skv_copy_chained scratch (kChainScratchBytes, allocated on first use)
+};
+
+/// skv_copy_chained scratch per device: landed-tile counters of up to SKV_COPY_MAX_SEGMENTS chunks, then the
+/// 8-byte tile-claim counter.
+constexpr size_t kChainScratchBytes = 4 * SKV_COPY_MAX_SEGMENTS + 8;
+
+/// Chaining of one TMA launch (skv_copy_chained): segment c of the plan is chunk c.
+struct ChainArgs {
+    const uint64_t* wait_flags;   // chunk c is loaded only once wait_flags[c] >= value (null: no waits)
+    uint64_t* signal_flags;       // chunk c landed: release store of value to signal_flags[c] (null: none)
+    uint32_t* landed;             // per-chunk landed-tile counters, zeroed in stream order before the launch
+    unsigned long long* next_tile;   // the tile-claim counter, zeroed with them
+    uint64_t value;
+    uint64_t timeout_ns;
 };
 /// Returns the context of the CURRENT device, creating it on first use.  Null on failure (error set).
 DeviceCtx* current_ctx();
@@ -75,6 +91,9 @@ int cuda_fail(cudaError_t e, const char* what);
 
 /// Launch one copy kernel for a prepared plan.  `engine` is SKV_COPY_TMA or SKV_COPY_VEC.
 int launch_copy(const CopyPlan& plan, uint64_t total_tiles, int engine, DeviceCtx& ctx, cudaStream_t stream);
+/// Launch the chained TMA kernel (the counters are reset on `stream` first).
+int launch_copy_chained(const CopyPlan& plan, uint64_t total_tiles, const ChainArgs& chain, DeviceCtx& ctx,
+                        cudaStream_t stream);
 /// Enqueue the flag kernels.
 int launch_signal(uint64_t* flag, uint64_t value, cudaStream_t stream);
 int launch_wait(const uint64_t* flag, uint64_t value, uint64_t timeout_ns, uint32_t* status, cudaStream_t stream);

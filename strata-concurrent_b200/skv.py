@@ -65,6 +65,7 @@ _SIGNATURES = {
     "skv_expand_block_table": ([C.c_void_p, C.c_int64, C.c_int64, C.c_int64, C.c_int64, C.c_void_p], C.c_int),
     "skv_copy": ([C.c_void_p, C.c_int, C.c_int, C.c_void_p], C.c_int),
     "skv_copy_noalloc": ([C.c_void_p, C.c_int, C.c_void_p, C.c_void_p], C.c_int),
+    "skv_copy_chained": ([C.c_void_p, C.c_int, C.c_void_p, C.c_void_p, C.c_uint64, C.c_uint64, C.c_void_p], C.c_int),
     "skv_set_copy_tuning": ([C.c_int, C.c_uint32, C.c_int, C.c_int], C.c_int),
     "skv_get_copy_tuning": ([C.POINTER(C.c_int), C.POINTER(C.c_uint32), C.POINTER(C.c_int), C.POINTER(C.c_int)], C.c_int),
     "skv_query_status": ([C.c_int, C.c_void_p, C.POINTER(C.c_uint32)], C.c_int),
@@ -136,12 +137,43 @@ def segment(src, dst, nbytes: int, *, src_pages=None, dst_pages=None, page_bytes
                    int(src_page_limit), int(dst_page_limit))
 
 
+def split_segment(seg: Segment, max_bytes: int) -> list:
+    """Cut one segment into pieces of at most `max_bytes` (whole pages for a paged side, 16-byte multiples for a
+    contiguous one), in order: the pieces move exactly the bytes of the whole.  Used to pipeline a long copy
+    chunk by chunk (a relay or a chained fan-out signals each piece as it lands)."""
+    paged = bool(seg.src_pages or seg.dst_pages)
+    unit = seg.page_bytes if paged else 16
+    if unit <= 0 or seg.bytes % unit:
+        raise ValueError("a segment splits on whole pages (paged) or 16-byte units (contiguous)")
+    per = max(1, max_bytes // unit) * unit
+    out = []
+    for at in range(0, seg.bytes, per):
+        n = min(per, seg.bytes - at)
+        first_page = at // unit if paged else 0
+        out.append(Segment(
+            seg.src if seg.src_pages else seg.src + at,
+            seg.dst if seg.dst_pages else seg.dst + at,
+            seg.src_pages + 4 * first_page if seg.src_pages else None,
+            seg.dst_pages + 4 * first_page if seg.dst_pages else None,
+            n, seg.page_bytes, 0, seg.src_page_limit, seg.dst_page_limit))
+    return out
+
+
 def copy(segs: list, engine: int = COPY_AUTO, stream=None) -> None:
     """ONE kernel launch moving every segment (gather, scatter, pool->pool, state rows, P2P, host)."""
     for i in range(0, max(len(segs), 1), MAX_SEGMENTS):
         chunk = segs[i:i + MAX_SEGMENTS]
         arr = (Segment * len(chunk))(*chunk)
         check(lib().skv_copy(arr, len(chunk), engine, _stream(stream)))
+
+
+def copy_chained(segs: list, wait_flags=None, signal_flags=None, value: int = 1, timeout_ns: int = 0,
+                 stream=None) -> None:
+    """One TMA launch moving `segs` as a pipeline of chunks (segment c = chunk c): chunk c waits for
+    wait_flags[c] >= value and, once landed, stores value to signal_flags[c] (flag arrays of 8-byte words)."""
+    arr = (Segment * len(segs))(*segs)
+    check(lib().skv_copy_chained(arr, len(segs), _ptr(wait_flags), _ptr(signal_flags), int(value), int(timeout_ns),
+                                 _stream(stream)))
 
 
 def set_copy_tuning(tma_stages: int, tma_tile_bytes: int, tma_ctas_per_sm: int, vec_ctas_per_sm: int) -> None:
