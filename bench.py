@@ -55,8 +55,10 @@ def parse():
     ap.add_argument("--seed", type=int, default=1)
     ap.add_argument("--pool-blocks", type=int, default=4096, help="slots per pool (the configs use 4,096)")
     ap.add_argument("--p2p", default="pull", choices=["pull", "push"], help="N > 1: which GPU runs the copy")
-    ap.add_argument("--scenario", default="pairs", choices=["pairs", "fanout"],
-                    help="N > 1: prefill/decode pairs (configs 3/5) or one prefill fanned out to N-1 decodes (config 4)")
+    ap.add_argument("--scenario", default="auto", choices=["auto", "pairs", "fanout", "mixed"],
+                    help="N > 1: pairs = N/2 prefill->decode pairs; fanout = one prefill to N-1 decodes (config 4); "
+                         "mixed = N/2 prefill + N/2 decode GPUs, 64 log-uniform sequences, host parks (config 5); "
+                         "auto = pairs, plus config 4 at N = 4 and config 5 at N = 8 embedded in the same line")
     ap.add_argument("--chunk-mb", type=int, default=32, help="fan-out chain: pipeline chunk size")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -536,7 +538,7 @@ def summarize_pairs(max_elapsed_ms: float, per_step_ms: np.ndarray, pairs: int, 
             "p50_ms": float(np.percentile(per_step_ms, 50)), "p99_ms": float(np.percentile(per_step_ms, 99))}
 
 
-def run_pairs(args, torch) -> None:
+def run_pairs(args, torch) -> dict | None:
     """N/2 prefill->decode pairs.  pull (default): the decode GPU's copy kernel reads the prefill GPU's pool
     pages over NVLink (TMA bulk loads from peer memory, no multicast) and writes its own pool; push: the
     prefill GPU's vector kernel stores into the decode GPU's pool.  Either way the destination slots are written
@@ -545,11 +547,7 @@ def run_pairs(args, torch) -> None:
     raises DONE on the prefill GPU (whose blocks may then be freed), prefill waits DONE; push = prefill pushes
     and raises ARRIVED, decode waits ARRIVED."""
     import torch.distributed as dist
-    from datetime import timedelta
-    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
-    local = int(os.environ.get("LOCAL_RANK", rank))
-    torch.cuda.set_device(local)
-    dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+    rank, world, local = ranks()
     kg = skv.KvGeometry()
     t = args.tokens
     pairs = world // 2
@@ -644,6 +642,7 @@ def run_pairs(args, torch) -> None:
             ok[0] = float(bool(torch.equal(got, image)))
     dist.all_reduce(ok, op=dist.ReduceOp.MIN)
     res = summarize_pairs(float(red[0].item()), per.cpu().numpy(), pairs, kg.metric_bytes(t), args.steps)
+    line = None
     if rank == 0:
         line = {"metric": METRIC, "value": round(res["value"], 3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": round(res["ms_per_step"], 4), "p50_ms": round(res["p50_ms"], 4),
@@ -661,18 +660,17 @@ def run_pairs(args, torch) -> None:
                              "peak_kind": "measured peer copy per direction (profiling recipe); 900 nominal",
                              "traffic": None, "kernel": "copy_tma_kernel" if pull else "copy_vec_kernel"},
                 "clocks": clk.summary()}
-        print(json.dumps(line))
     torch.cuda.synchronize()
     dist.barrier()
     for p in imported:
         skv.ipc_close(p)
     dist.barrier()
-    dist.destroy_process_group()
+    return line if rank == 0 else None
 
 
 # ------------------------------------------------------------------------------------------------ fan-out
 
-def run_fanout(args, torch) -> None:
+def run_fanout(args, torch, tokens: int | None = None, steps: int | None = None) -> dict | None:
     """Config 4: rank 0 (prefill) holds one sequence; ranks 1..N-1 (decode) each receive the whole cache into
     their own pool at independent random slots.  Three ways, each timed over the same K steps:
 
@@ -685,13 +683,10 @@ def run_fanout(args, torch) -> None:
 
     value = receivers x B(T) x K / max-over-ranks timed region (fan-out counts every receiver's bytes)."""
     import torch.distributed as dist
-    from datetime import timedelta
-    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
-    local = int(os.environ.get("LOCAL_RANK", rank))
-    torch.cuda.set_device(local)
-    dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+    rank, world, local = ranks()
     kg = skv.KvGeometry()
-    t = args.tokens
+    t = tokens or args.tokens
+    n_steps = steps or n_steps
     receivers = world - 1
     lay = state_layout(kg, t)
     stream = torch.cuda.current_stream()
@@ -732,15 +727,15 @@ def run_fanout(args, torch) -> None:
             step()
         torch.cuda.synchronize()
         dist.barrier()
-        ev = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(n_steps + 1)]
         ev[0].record(stream)
-        for i in range(args.steps):
+        for i in range(n_steps):
             step()
             ev[i + 1].record(stream)
         torch.cuda.synchronize()
         dist.barrier()
-        per = torch.tensor([ev[i].elapsed_time(ev[i + 1]) for i in range(args.steps)], device="cuda")
-        tot = torch.tensor([ev[0].elapsed_time(ev[args.steps])], device="cuda")
+        per = torch.tensor([ev[i].elapsed_time(ev[i + 1]) for i in range(n_steps)], device="cuda")
+        tot = torch.tensor([ev[0].elapsed_time(ev[n_steps])], device="cuda")
         dist.all_reduce(tot, op=dist.ReduceOp.MAX)
         dist.all_reduce(per, op=dist.ReduceOp.MAX)
         return float(tot.item()), per.cpu().numpy()
@@ -845,17 +840,18 @@ def run_fanout(args, torch) -> None:
     dist.all_reduce(status, op=dist.ReduceOp.MAX)
 
     b = kg.metric_bytes(t)
+    line = None
     if rank == 0:
         methods = {}
         for name, (tot, per, ok) in results.items():
-            methods[name] = {"value": round(receivers * b * args.steps / (tot / 1e3) / 1e9, 3),
-                             "ms_per_step": round(tot / args.steps, 4),
+            methods[name] = {"value": round(receivers * b * n_steps / (tot / 1e3) / 1e9, 3),
+                             "ms_per_step": round(tot / n_steps, 4),
                              "p50_ms": round(float(np.percentile(per, 50)), 4),
                              "p99_ms": round(float(np.percentile(per, 99)), 4),
-                             "per_receiver_gbs": round(b * args.steps / (tot / 1e3) / 1e9, 3), "parity": ok}
+                             "per_receiver_gbs": round(b * n_steps / (tot / 1e3) / 1e9, 3), "parity": ok}
         best = max(methods, key=lambda k: methods[k]["value"])
         m = methods[best]
-        line = {"metric": METRIC, "value": m["value"], "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        line = {"metric": METRIC, "value": m["value"], "unit": UNIT, "n_gpus": world, "steps": n_steps,
                 "warmup": args.warmup, "ms_per_step": m["ms_per_step"], "p50_ms": m["p50_ms"], "p99_ms": m["p99_ms"],
                 "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u8", "data": "synthetic",
                 "config": {"workload": f"config 4: 1 prefill GPU fans one {t}-token cache out to {receivers} decode "
@@ -867,14 +863,251 @@ def run_fanout(args, torch) -> None:
                              "unit": "GB/s", "frac": round(m["per_receiver_gbs"] / NVLINK_PEER_COPY_GBS, 4),
                              "peak_kind": "measured peer copy per direction; each receiver's ingress",
                              "traffic": None, "kernel": "copy_tma_kernel"}}
-        print(json.dumps(line))
     torch.cuda.synchronize()
     dist.barrier()
     for pool, state in maps.values():
         skv.ipc_close(pool)
         skv.ipc_close(state)
     dist.barrier()
-    dist.destroy_process_group()
+    return line if rank == 0 else None
+
+
+# ------------------------------------------------------------------------------------------------ mixed (config 5)
+
+MIXED_SEQUENCES = 64
+MIXED_TOKENS = (1024, 131072)      # log-uniform lengths (mean ~26.8K tokens)
+SERVE_SLOTS = 8                    # serve slots per decode GPU, parked to and resumed from host during the handoffs
+SLOT_TOKENS = 4096
+
+
+def mixed_plan(world: int, seed: int) -> dict:
+    """Config 5's workload, identical on every rank: seeded log-uniform lengths on [1K, 128K], each sequence's
+    prefill owner (an even rank) and decode target (an odd rank) drawn at random."""
+    rng = np.random.default_rng(seed)
+    lo, hi = MIXED_TOKENS
+    lengths = np.exp(rng.uniform(np.log(lo), np.log(hi), MIXED_SEQUENCES)).astype(np.int64)
+    prefill = [r for r in range(world) if r % 2 == 0]
+    decode = [r for r in range(world) if r % 2 == 1]
+    return {"lengths": [int(x) for x in lengths], "owner": [int(x) for x in rng.choice(prefill, MIXED_SEQUENCES)],
+            "target": [int(x) for x in rng.choice(decode, MIXED_SEQUENCES)]}
+
+
+class SeqSet:
+    """Several sequences in ONE library-allocated block pool (CUDA-IPC exportable) plus one state arena with each
+    sequence's GDN rows and ids (`state_layout` per sequence), every layer's blocks at seed-random slots."""
+
+    def __init__(self, torch, kg: skv.KvGeometry, lengths: list, seed: int, fill: bool):
+        dev = torch.cuda.current_device()
+        self.kg, self.lengths = kg, list(lengths)
+        self.n_blocks = sum(kg.n_qsa * kg.blocks(t) for t in lengths) + 1
+        self.pool = skv.Pool(dev, self.n_blocks, kg.block_bytes)
+        self.offs, at = [], 0
+        for t in lengths:
+            self.offs.append(at)
+            at += state_layout(kg, t)["bytes"]
+        self.state_bytes = max(at, 1024)
+        self.state = skv.Pool(dev, 1, self.state_bytes)
+        gen = torch.Generator(device="cuda").manual_seed(seed)
+        chunk = 256 << 20
+        for base, total, floats in ((self.pool.base, self.n_blocks * kg.block_bytes, False),
+                                    (self.state.base, self.state_bytes, True)):
+            for a in range(0, total, chunk):
+                n = min(chunk, total - a)
+                if not fill:
+                    r = torch.zeros(n, dtype=torch.uint8, device="cuda")
+                elif floats:
+                    r = torch.randn(n // 4, generator=gen, device="cuda") * 0.02
+                else:
+                    r = torch.randn(n // 2, generator=gen, device="cuda", dtype=torch.float16)
+                skv.copy([skv.segment(r, base + a, n)], skv.COPY_VEC)
+                torch.cuda.synchronize()
+        self.pool.scramble(seed)
+        self.blocks = [np.stack([self.pool.alloc(kg.blocks(t)) for _ in range(kg.n_qsa)]) for t in lengths]
+        self.tables = [torch.from_numpy(skv.PooledSequence.host_tables(kg, b).reshape(-1).copy()).cuda()
+                       for b in self.blocks]
+        self.seqs = [self.view(i, self.pool, self.state.base, self.tables[i]) for i in range(len(lengths))]
+
+    def view(self, i: int, pool: skv.Pool, state_base: int, tables) -> skv.PooledSequence:
+        t = self.lengths[i]
+        lay = state_layout(self.kg, t)
+        return skv.PooledSequence(self.kg, pool, t, self.kg.n_qsa, self.blocks[i] if pool is self.pool else None,
+                                  tables, state_base + self.offs[i], state_base + self.offs[i] + lay["ids"])
+
+
+def run_mixed(args, torch) -> dict | None:
+    """Config 5: the even ranks prefill, the odd ranks decode.  64 sequences with seeded log-uniform lengths on
+    [1K, 128K] live in their prefill owner's pool; each decode GPU pulls the sequences assigned to it (random
+    pairing, so several decode GPUs may read one prefill GPU at once) back to back, one skv_copy (TMA, peer
+    loads, no multicast) per sequence straight into its own pool.  Meanwhile a side stream on every decode GPU
+    parks its 8 serve slots (4,096-token conversations) to pinned host memory and resumes them (skv_park /
+    skv_resume, staged).  value = all 64 sequences' B(T) per step / the max-over-ranks handoff window; the
+    per-sequence latency is each pull's device time."""
+    import torch.distributed as dist
+    rank, world, local = ranks()
+    kg = skv.KvGeometry()
+    plan = mixed_plan(world, args.seed)
+    lengths, owner, target = plan["lengths"], plan["owner"], plan["target"]
+    steps, warmup = min(args.steps, 5), max(1, min(args.warmup, 2))
+    stream = torch.cuda.current_stream()
+    sp = stream.cuda_stream
+    L = skv.lib()
+    mine_out = [i for i in range(MIXED_SEQUENCES) if owner[i] == rank]
+    mine_in = [i for i in range(MIXED_SEQUENCES) if target[i] == rank]
+    decode = rank % 2 == 1
+    # prefill side: its sequences resident; decode side: room for what it receives, plus its serve slots
+    held = SeqSet(torch, kg, [lengths[i] for i in (mine_in if decode else mine_out)], args.seed + 7 * rank,
+                  fill=not decode)
+    slots = SeqSet(torch, kg, [SLOT_TOKENS] * (2 * SERVE_SLOTS), args.seed + 7 * rank + 3, fill=True) if decode else None
+    info = None if decode else {"pool": skv.ipc_export(held.pool.base), "state": skv.ipc_export(held.state.base),
+                                "n_blocks": held.n_blocks, "seqs": mine_out, "offs": held.offs, "blocks": held.blocks}
+    torch.cuda.synchronize()
+    infos = [None] * world
+    dist.all_gather_object(infos, info)
+    maps, keep, pulls = {}, [], []
+    for k, i in enumerate(mine_in if decode else []):
+        p = owner[i]
+        if p not in maps:
+            maps[p] = (skv.ipc_import(local, infos[p]["pool"]), skv.ipc_import(local, infos[p]["state"]))
+        pool_base, state_base = maps[p]
+        j = infos[p]["seqs"].index(i)
+        t = lengths[i]
+        blocks = infos[p]["blocks"][j]
+        tables = torch.from_numpy(skv.PooledSequence.host_tables(kg, blocks).reshape(-1).copy()).cuda()
+        peer_pool = skv.Pool(local, infos[p]["n_blocks"], kg.block_bytes, memory=pool_base)
+        lay = state_layout(kg, t)
+        src = skv.PooledSequence(kg, peer_pool, t, kg.n_qsa, None, tables, state_base + infos[p]["offs"][j],
+                                 state_base + infos[p]["offs"][j] + lay["ids"])
+        dst = held.seqs[k]
+        segs = skv.kv_segments_pool_to_pool(src, dst) + skv.state_segments(src, dst.gdn, dst.ids)
+        keep += [tables, peer_pool]
+        pulls.append((i, (skv.Segment * len(segs))(*segs), len(segs)))
+    side = torch.cuda.Stream()
+    if decode:
+        off = skv.image_offsets(kg, SLOT_TOKENS, kg.n_qsa)
+        hosts = [skv.HostBuffer(off["total"]) for _ in range(SERVE_SLOTS)]
+        staging = torch.empty(off["total"] + 256 * 64, dtype=torch.uint8, device="cuda")
+        park_segs = [skv.pack_segments(slots.seqs[j], hosts[j].ptr) for j in range(SERVE_SLOTS)]
+        resume_segs = [skv.unpack_segments(hosts[j].ptr, slots.seqs[SERVE_SLOTS + j]) for j in range(SERVE_SLOTS)]
+    lat = []       # per-sequence pull times (ms), timed steps
+    windows = []   # (handoff window, park window) per timed step, this rank
+    for it in range(warmup + steps):
+        dist.barrier()
+        torch.cuda.synchronize()
+        h0, h1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in pulls]
+        h0.record(stream)
+        side.wait_stream(stream)
+        p0.record(side)
+        if decode:
+            for j in range(SERVE_SLOTS):
+                skv.park(park_segs[j], skv.PARK_STAGED, staging, staging.numel(), side)
+                skv.resume(resume_segs[j], skv.PARK_STAGED, staging, staging.numel(), side)
+        p1.record(side)
+        for (i, arr, n), (a, b) in zip(pulls, ev):
+            a.record(stream)
+            skv.check(L.skv_copy(arr, n, skv.COPY_TMA, sp))
+            b.record(stream)
+        h1.record(stream)
+        torch.cuda.synchronize()
+        if it >= warmup:
+            windows.append((h0.elapsed_time(h1), p0.elapsed_time(p1)))
+            lat += [a.elapsed_time(b) for a, b in ev]
+    status = torch.tensor([float(skv.query_status(local) != 0)], device="cuda")
+    dist.all_reduce(status, op=dist.ReduceOp.MAX)
+    win = torch.tensor([w[0] for w in windows], device="cuda")
+    dist.all_reduce(win, op=dist.ReduceOp.MAX)
+    # parity: every handed-off sequence, packed through the decode GPU's table, equals its prefill original; every
+    # resumed serve slot equals the slot it was parked from
+    ok = True
+    for i in range(MIXED_SEQUENCES):
+        p, d = owner[i], target[i]
+        if rank == d:
+            img = pack_image(torch, held.seqs[mine_in.index(i)])
+            dist.send(img, p)
+            del img
+        elif rank == p:
+            img = pack_image(torch, held.seqs[mine_out.index(i)])
+            got = torch.empty_like(img)
+            dist.recv(got, d)
+            ok = ok and bool(torch.equal(img, got))
+            del img, got
+    if decode:
+        for j in range(SERVE_SLOTS):
+            ok = ok and bool(torch.equal(pack_image(torch, slots.seqs[j]), pack_image(torch, slots.seqs[SERVE_SLOTS + j])))
+    okt = torch.tensor([float(ok)], device="cuda")
+    dist.all_reduce(okt, op=dist.ReduceOp.MIN)
+    # gather per-rank facts to rank 0
+    facts = {"lat": lat, "park_ms": [w[1] for w in windows], "hand_ms": [w[0] for w in windows],
+             "bytes_in": sum(kg.metric_bytes(lengths[i]) for i in mine_in), "decode": decode}
+    allf = [None] * world
+    dist.all_gather_object(allf, facts)
+    torch.cuda.synchronize()
+    dist.barrier()
+    del pulls, keep
+    for pool_base, state_base in maps.values():
+        skv.ipc_close(pool_base)
+        skv.ipc_close(state_base)
+    dist.barrier()
+    if rank != 0:
+        return None
+    total = sum(kg.metric_bytes(t) for t in lengths)
+    wins = win.cpu().numpy()
+    value = total * steps / (float(wins.sum()) / 1e3) / 1e9
+    lat_all = np.concatenate([np.asarray(f["lat"]) for f in allf if f["lat"]])
+    slot_bytes = 2 * SERVE_SLOTS * kg.metric_bytes(SLOT_TOKENS)
+    dec = [f for f in allf if f["decode"]]
+    per_decode = [round(f["bytes_in"] / (np.mean(f["hand_ms"]) / 1e3) / 1e9, 1) for f in dec]
+    parks = [round(slot_bytes / (np.mean(f["park_ms"]) / 1e3) / 1e9, 2) for f in dec]
+    mean_ingress = float(np.mean(per_decode))
+    return {"metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world, "steps": steps, "warmup": warmup,
+            "ms_per_step": round(float(wins.mean()), 4), "p50_ms": round(float(np.percentile(lat_all, 50)), 4),
+            "p99_ms": round(float(np.percentile(lat_all, 99)), 4), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "u8", "data": "synthetic",
+            "config": {"workload": f"config 5: {world // 2} prefill + {world // 2} decode GPUs, {MIXED_SEQUENCES} "
+                                   f"sequences with seeded log-uniform lengths on [1K, 128K] tokens, random "
+                                   f"prefill->decode pairing, pulled over NVLink straight into the decode pools while "
+                                   f"{SERVE_SLOTS} serve slots of {SLOT_TOKENS} tokens per decode GPU park to and "
+                                   f"resume from pinned host memory",
+                       "sequences": MIXED_SEQUENCES, "mean_tokens": round(float(np.mean(lengths)), 1),
+                       "bytes_per_step": total, "serve_slots": SERVE_SLOTS, "slot_tokens": SLOT_TOKENS,
+                       "parallelism": f"{world // 2} prefill + {world // 2} decode"},
+            "handoffs": {"per_decode_gpu_gbs": per_decode, "p50_ms": round(float(np.percentile(lat_all, 50)), 4),
+                         "p99_ms": round(float(np.percentile(lat_all, 99)), 4),
+                         "max_ms": round(float(lat_all.max()), 4), "note": "per-sequence device time of its pull"},
+            "parks": {"per_decode_gpu_gbs": parks, "bytes_per_step_per_gpu": slot_bytes,
+                      "note": "park + resume of every serve slot, staged, on a side stream during the handoffs"},
+            "parity": bool(okt.item() == 1.0) and status.item() == 0,
+            "gpu_launches": steps * (MIXED_SEQUENCES + len(dec) * SERVE_SLOTS * 2),
+            "roofline": {"bound": "nvlink", "achieved": round(mean_ingress, 1), "peak": NVLINK_PEER_COPY_GBS,
+                         "unit": "GB/s", "frac": round(mean_ingress / NVLINK_PEER_COPY_GBS, 4),
+                         "peak_kind": "measured peer copy per direction; mean decode-GPU ingress over its window",
+                         "traffic": None, "kernel": "copy_tma_kernel"}}
+
+
+def pack_image(torch, ps: skv.PooledSequence):
+    """A sequence packed through its own table (K/V, GDN rows, ids) by the gather kernel."""
+    off = skv.image_offsets(ps.g, ps.tokens, ps.layers)
+    image = torch.zeros(off["total"], dtype=torch.uint8, device="cuda")
+    skv.copy(skv.pack_segments(ps, image), skv.COPY_TMA)
+    torch.cuda.synchronize()
+    return image
+
+
+def ranks() -> tuple:
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    return rank, world, int(os.environ.get("LOCAL_RANK", rank))
+
+
+def brief(line: dict | None, keys=("value", "ms_per_step", "p50_ms", "p99_ms", "parity")) -> dict | None:
+    """The headline fields of a scenario's line, plus its config and method table, for embedding."""
+    if line is None:
+        return None
+    out = {k: line[k] for k in keys if k in line}
+    for k in ("config", "methods", "roofline", "handoffs", "parks"):
+        if k in line:
+            out[k] = line[k]
+    return out
 
 
 def main() -> None:
@@ -884,12 +1117,36 @@ def main() -> None:
         return
     import torch
     world = int(os.environ.get("WORLD_SIZE", "1"))
-    if world > 1 and args.scenario == "fanout":
-        run_fanout(args, torch)
-    elif world > 1:
-        run_pairs(args, torch)
-    else:
+    if world == 1:
         run_single(args, torch)
+        return
+    import torch.distributed as dist
+    from datetime import timedelta
+    rank, world, local = ranks()
+    torch.cuda.set_device(local)
+    dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+    try:
+        if args.scenario == "fanout":
+            line = run_fanout(args, torch)
+        elif args.scenario == "mixed":
+            line = run_mixed(args, torch)
+        else:
+            # the headline: N/2 pairs (configs 3/5 throughput, weak scaling); at N = 4 and N = 8 the same run also
+            # measures BASELINE's own 4- and 8-GPU configs and embeds them
+            line = run_pairs(args, torch)
+            if args.scenario == "auto" and world == 4:
+                sub = run_fanout(args, torch, tokens=65536, steps=min(args.steps, 40))
+                if line is not None:
+                    line["config4_fanout"] = brief(sub)
+            if args.scenario == "auto" and world == 8:
+                sub = run_mixed(args, torch)
+                if line is not None:
+                    line["config5_mixed"] = brief(sub)
+        if rank == 0 and line is not None:
+            print(json.dumps(line))
+    finally:
+        torch.cuda.synchronize()
+        dist.destroy_process_group()
 
 
 if __name__ == "__main__":

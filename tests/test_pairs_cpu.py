@@ -31,6 +31,18 @@ def test_state_layout():
         assert lay["flag"] + 8 <= lay["bytes"] and lay["bytes"] % 1024 == 0
 
 
+def test_mixed_plan_is_seeded_and_log_uniform():
+    a, b = bench.mixed_plan(8, 1), bench.mixed_plan(8, 1)
+    assert a == b and a != bench.mixed_plan(8, 2)
+    lengths = np.asarray(a["lengths"])
+    assert len(lengths) == bench.MIXED_SEQUENCES
+    assert lengths.min() >= bench.MIXED_TOKENS[0] and lengths.max() <= bench.MIXED_TOKENS[1]
+    assert set(a["owner"]) <= {0, 2, 4, 6} and set(a["target"]) <= {1, 3, 5, 7}
+    # the log-uniform mean over [1K, 128K] is (128K - 1K) / ln 128 ~ 26.8K; many seeds stay near it
+    means = [np.mean(bench.mixed_plan(8, s)["lengths"]) for s in range(40)]
+    assert 20000 < np.mean(means) < 34000
+
+
 def test_summarize_pairs():
     per = np.linspace(1.0, 2.0, 100)
     r = bench.summarize_pairs(150.0, per, pairs=4, seq_bytes=10 ** 9, steps=100)
