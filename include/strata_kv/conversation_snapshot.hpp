@@ -5,19 +5,22 @@
 // snapshots with and without a layer split; validate-before-write; transfer_failed after the first write).
 //
 // What the B200 build changes underneath:
-//   * every layer's K/V is read and written THROUGH QsaState::page_table, so a pool placed by a block allocator
-//     (non-identity table) parks and mounts exactly like the reference's identity pool, byte for byte;
+//   * a block-pool layer's K/V is read and written THROUGH QsaState::page_table, so a pool placed by a block
+//     allocator (non-identity table) parks and mounts exactly like the reference's identity pool, byte for byte;
 //   * the bytes move with the sm_100a copy kernels: one gather launch per device collects every layer's streams
 //     and the running state into a device staging image, the copy engine moves it into pinned host segments, and
 //     a mount is the reverse (one scatter launch);
 //   * the whole-session save / restore issue one batch (and one synchronisation) per device, not one synchronous
 //     copy per 16 MiB segment.
-// Streamed layers (kv_mode 1 / 2) save from their authoritative host pools like the reference does; restoring
-// them needs the streamed-mode residency movers, which this build does not have, so such a restore is refused
-// before anything is written.
+// Streamed layers (kv_mode 1 / 2) keep their authoritative K/V in pinned host memory, as in the reference: a park
+// copies it, a mount writes it back and then evicts every VRAM block (kv_mode 1, kv_stream_reset) or refills the
+// ring's last n_slots pages (kv_mode 2), with the block movers of include/strata_kv/kv_stream.hpp.  A resident
+// layer in a block pool (skv_pool_create / skv_pool_wrap) is addressed through its page table; any other resident
+// layer is identity-addressed, which is what the reference assumes.
 #pragma once
 
 #include "strata_kv/conversation_cache.hpp"
+#include "strata_kv/kv_stream.hpp"
 #include "strata_kv/types.hpp"
 
 #include <string>

@@ -47,12 +47,57 @@ struct KvStreamMap {
 
 enum KvFormat : int { kKvF16 = 0, kKvInt8 = 1, kKvQ4 = 2 };
 
-/// The reference's fixed QSA shapes this path depends on (include/strata/kernels/qsa.hpp:95-117).
+/// The QSA shapes (include/strata/kernels/qsa.hpp:96-117): zero by default, the real artifact's from
+/// qsa_real_shapes().
 struct QsaShapes {
-    int64_t idx_block = 4;   ///< the indexer pools one key per 4 cells
-    int64_t page_size = 4;   ///< KV page granule in cells
+    int64_t n_head = 0;
+    int64_t n_head_kv = 0;
+    int64_t head_dim = 0;
+    int64_t n_rot = 0;
+    int64_t idx_n_head = 0;
+    int64_t idx_dim = 0;
+    int64_t idx_block = 0;   ///< the indexer pools one key per idx_block cells
+    int64_t idx_top_k = 0;
+    int64_t page_size = 0;   ///< KV page granule in cells
 };
-inline QsaShapes qsa_real_shapes() { return {}; }
+inline QsaShapes qsa_real_shapes() {
+    QsaShapes s;
+    s.n_head = 24;
+    s.n_head_kv = 2;
+    s.head_dim = 256;
+    s.n_rot = 64;
+    s.idx_n_head = 4;
+    s.idx_dim = 128;
+    s.idx_block = 4;
+    s.idx_top_k = 2048;
+    s.page_size = 4;
+    return s;
+}
+
+/// The per-query step record of the capturable QSA kernels (include/strata/kernels/qsa.hpp:156-162): the
+/// selection width of query q is steps[q * kStepCount + kStepWidth].
+enum QsaStep : int { kStepWidth = 3, kStepCount = 4 };
+
+/// The pools a QSA reader addresses through `page_table` (include/strata/kernels/qsa_decode_attn.hpp:23-33).
+struct QsaAttnPools {
+    const uint16_t* k_pool = nullptr;
+    const uint16_t* v_pool = nullptr;
+    const int8_t* k_q = nullptr;
+    const int8_t* v_q = nullptr;
+    const uint16_t* k_scale = nullptr;
+    const uint16_t* v_scale = nullptr;
+    const uint8_t* k_q4 = nullptr;
+    const uint8_t* v_q4 = nullptr;
+    const int32_t* page_table = nullptr;
+};
+
+/// INT8 KV: one fp16 scale per 64 values (include/strata/kernels/kv_q8.hpp:22).
+inline constexpr int KV_Q8_GROUP = 64;
+
+/// The streaming map's control words: [0] epoch [1] hand [2] misses of the last call [3] overflow, u64 counters at
+/// [4] misses, [6] lookups, [8] calls (include/strata/kernels/kv_stream.hpp:61).
+inline constexpr int kKvCtlInts = 16;
+inline uint64_t kv_stream_map_bytes(int64_t n_slots) { return (uint64_t) n_slots * 4 * 5 + kKvCtlInts * 4; }
 
 /// Q4_0 rotated KV: 18-byte blocks of 32 values (include/strata/kernels/kv_q4.hpp:33).
 inline uint64_t kv_q4_bytes_per_head(int head_dim) { return (uint64_t) (head_dim / 32) * 18u; }
@@ -90,8 +135,9 @@ struct ModelGeometry {
 };
 
 /// One QSA layer's persistent state: the paged K/V pools with their page table, and the indexer rows.
-/// `page_table` (device int32, logical page -> physical page) is honoured by every copy of this path, so a
-/// block-pool placement (include/strata_kv.h skv_expand_block_table) and the reference's identity table both work.
+/// A resident (kv_mode 0) layer whose pools lie inside a block pool created with skv_pool_create / skv_pool_wrap is
+/// parked and mounted THROUGH `page_table` (device int32, logical page -> physical page), so a block-allocator
+/// placement works; any other resident layer is identity-addressed, exactly as the reference assumes in mode 0.
 struct QsaState {
     uint16_t* k_pool = nullptr;
     uint16_t* v_pool = nullptr;
@@ -120,6 +166,29 @@ struct QsaState {
 
 inline int qsa_kv_format(const QsaState& st) {
     return st.kv_q4 ? strata::kernels::kKvQ4 : st.kv_int8 ? strata::kernels::kKvInt8 : strata::kernels::kKvF16;
+}
+
+/// The pools a reader of this layer addresses (the reference's src/core/layer.cpp:710-718).
+inline strata::kernels::QsaAttnPools qsa_attn_pools(const QsaState& st) {
+    strata::kernels::QsaAttnPools p;
+    p.page_table = st.page_table;
+    if (st.kv_hybrid) {
+        p.k_q = st.k_q;
+        p.k_scale = st.k_scale;
+        p.v_q4 = st.v_q4;
+    } else if (st.kv_q4) {
+        p.k_q4 = st.k_q4;
+        p.v_q4 = st.v_q4;
+    } else if (st.kv_int8) {
+        p.k_q = st.k_q;
+        p.v_q = st.v_q;
+        p.k_scale = st.k_scale;
+        p.v_scale = st.v_scale;
+    } else {
+        p.k_pool = st.k_pool;
+        p.v_pool = st.v_pool;
+    }
+    return p;
 }
 
 /// The per-sequence state a session owns: GDN rows, the QSA states of its layer carve, the PLE history.

@@ -158,3 +158,73 @@ uint64_t orc_page_checksum(const uint8_t* p, int64_t n_pages, uint64_t page_byte
     }
     return outer;
 }
+
+/* ---- the streaming residency resolve, restated sequentially (kv_oracle.h) ---- */
+int64_t orc_stream_resolve(int32_t* table, int32_t* slot_block, int32_t* slot_stamp, int32_t* slot_ref, int32_t* ctl,
+                           int32_t* miss_block, int32_t* miss_slot, int64_t n_blocks, int64_t n_slots,
+                           const int32_t* ids, const int32_t* steps, int64_t n_q, int64_t cap, int64_t page_size) {
+    const int32_t epoch = ctl[0] + 1;
+    int64_t n_miss = 0, lookups = 0;
+    int overflow = 0;
+    for (int64_t q = 0; q < n_q; ++q) {
+        int64_t width = steps[q * 4 + 3];
+        if (width > cap) width = cap;
+        const int32_t* qi = ids + q * cap;
+        for (int64_t i = 0; i < width; ++i) {
+            const int64_t b = qi[i] / page_size;
+            if (i > 0 && qi[i - 1] / page_size == b) continue;
+            if (b < 0 || b >= n_blocks) continue;
+            ++lookups;
+            const int32_t sl = table[b];
+            if (sl >= 0) {
+                slot_stamp[sl] = epoch;
+                slot_ref[sl] = 1;
+            } else if (sl == -1) {
+                if (n_miss < n_slots) {
+                    table[b] = -2;
+                    miss_block[n_miss] = (int32_t) b;
+                } else {
+                    overflow = 1;   /* more distinct misses than slots: the block stays evicted */
+                }
+                ++n_miss;
+            }
+        }
+    }
+    const int64_t need = n_miss < n_slots ? n_miss : n_slots;
+    int64_t hand = ctl[1], got = 0;
+    for (int64_t walked = 0; got < need && walked < 3 * n_slots; ++walked) {
+        const int64_t j = hand % n_slots;
+        hand = (hand + 1) % n_slots;
+        if (slot_stamp[j] == epoch) continue;
+        if (slot_block[j] < 0 || slot_ref[j] == 0) {
+            miss_slot[got++] = (int32_t) j;
+            slot_stamp[j] = epoch;
+        } else {
+            slot_ref[j] = 0;
+        }
+    }
+    for (int64_t k = 0; k < need; ++k) {
+        const int32_t b = miss_block[k];
+        if (k >= got) {
+            table[b] = -1;
+            continue;
+        }
+        const int32_t sl = miss_slot[k];
+        if (slot_block[sl] >= 0) table[slot_block[sl]] = -1;
+        slot_block[sl] = b;
+        slot_stamp[sl] = epoch;
+        slot_ref[sl] = 1;
+        table[b] = sl;
+    }
+    ctl[0] = epoch;
+    ctl[1] = (int32_t) hand;
+    ctl[2] = (int32_t) got;
+    if (got < n_miss || overflow) ctl[3] = 1;
+    uint64_t c[3];
+    memcpy(c, ctl + 4, sizeof c);
+    c[0] += (uint64_t) got;
+    c[1] += (uint64_t) lookups;
+    c[2] += 1;
+    memcpy(ctl + 4, c, sizeof c);
+    return got;
+}

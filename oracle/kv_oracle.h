@@ -68,6 +68,19 @@ uint64_t orc_fnv1a64(const uint8_t* p, uint64_t n, uint64_t seed);
  * page_sums[p] = FNV-1a of page p; the sequence checksum is FNV-1a over the page_sums array. */
 uint64_t orc_page_checksum(const uint8_t* p, int64_t n_pages, uint64_t page_bytes);
 
+/* ---- the streaming residency resolve (src/kernels/cuda/kv_stream.cu:82-158; policy: kv_stream.hpp:8-15) ----
+ * One call over host copies of the map arrays, sequentially: for each query q and each position i < width(q) that
+ * starts a block (ids ascending), a resident block takes `epoch = ctl[0] + 1` and its reference bit; a missing block
+ * (table -1) is claimed (-2) and appended to the miss list.  Then the CLOCK hand from ctl[1] walks the slots: a
+ * slot stamped this epoch is skipped, a free (block < 0) or unreferenced slot is taken for the next miss (stamped),
+ * any other slot it passes loses its reference bit; the hand stops just past the slot that takes the last miss, and
+ * walks at most 3 * n_slots slots.  Placed misses re-point the table (an evicted block goes to -1); unplaced ones
+ * go back to -1 and set ctl[3].  ctl[0] = epoch, ctl[1] = hand, ctl[2] = placed, u64 counters at ctl[4..9]
+ * (misses placed, lookups, calls).  Returns the number placed. */
+int64_t orc_stream_resolve(int32_t* table, int32_t* slot_block, int32_t* slot_stamp, int32_t* slot_ref, int32_t* ctl,
+                           int32_t* miss_block, int32_t* miss_slot, int64_t n_blocks, int64_t n_slots,
+                           const int32_t* ids, const int32_t* steps, int64_t n_q, int64_t cap, int64_t page_size);
+
 #ifdef __cplusplus
 }
 #endif

@@ -18,7 +18,7 @@ CSRC = os.path.join(HERE, "csrc")
 INCLUDE = os.path.join(ROOT, "include")
 LIB = os.path.join(HERE, "libstrata_kv.so")
 
-CUDA_SOURCES = ["skv_copy.cu", "skv_abi.cu"]
+CUDA_SOURCES = ["skv_copy.cu", "skv_abi.cu", "kv_stream.cu"]
 # the C++ drop-in layer (strata::core API), host code on top of the C ABI
 HOST_SOURCES = ["host/pinned.cpp", "host/transfer.cpp", "host/conversation_snapshot.cpp", "host/conversation_state.cpp",
                 "host/conversation_wire.cpp", "host/conversation_wire_device.cpp", "host/handoff.cpp"]

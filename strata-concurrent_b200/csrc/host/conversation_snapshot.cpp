@@ -3,9 +3,15 @@
 //
 // The extents and the refusal rules are the reference's (a layer's snapshot covers whole 4-cell pages up to
 // `upto`, K/V data and scales per format, and the indexer's pooled rows including the moving spare row); the
-// movement is this build's: every stream is read or written through QsaState::page_table by the copy kernels,
-// batched into one launch with the rest of the session (snapshot_detail::enqueue_*).
+// movement is this build's: every stream is read or written by the copy kernels - through QsaState::page_table
+// when the layer lives in a block pool - batched into one launch with the rest of the session
+// (snapshot_detail::enqueue_*).  Streamed (kv_mode 1) and ring (kv_mode 2) layers keep their authoritative K/V in
+// pinned host memory: a park copies it, a mount writes it back and then evicts every block (mode 1) or refills
+// the ring (mode 2), as the reference does (src/core/conversation_snapshot.cpp:190-206).
 #include "snapshot_detail.hpp"
+
+#include "kv_stream_detail.h"
+#include "skv_internal.h"
 
 #include <algorithm>
 #include <array>
@@ -100,10 +106,19 @@ std::array<const void*, 5> layer_sources(const QsaState& st) {
     return {host ? st.host.k_pool : st.k_pool, host ? st.host.v_pool : st.v_pool, nullptr, nullptr, st.idx_pooled};
 }
 
+std::array<const void*, 5> layer_slots(const QsaState& st) {
+    if (st.kv_hybrid) return {st.k_q, st.v_q4, st.k_scale, nullptr, st.idx_pooled};
+    if (st.kv_q4) return {st.k_q4, st.v_q4, nullptr, nullptr, st.idx_pooled};
+    if (st.kv_int8) return {st.k_q, st.v_q, st.k_scale, st.v_scale, st.idx_pooled};
+    return {st.k_pool, st.v_pool, nullptr, nullptr, st.idx_pooled};
+}
+
 strata::kv::DeviceStream layer_stream(const QsaState& st, const LayerExtent& x, int i, const void* base) {
     strata::kv::DeviceStream s;
     s.base = base;
-    if (i < 4 && st.kv_mode == 0 && st.page_table && x.cells > 0) {
+    // a block-pool layer is addressed through its table; any other resident layer is identity-addressed, which is
+    // what the reference assumes of every kv_mode 0 layer
+    if (i < 4 && st.kv_mode == 0 && st.page_table && x.cells > 0 && skv::in_block_pool(base)) {
         const int64_t pages = x.cells / x.page_size;
         s.pages = st.page_table;
         s.page_bytes = (uint32_t) (x.bytes[(size_t) i] / (size_t) pages);
@@ -150,15 +165,44 @@ bool enqueue_kv_save(ConversationKv& image, const QsaState& st, const ModelGeome
 bool enqueue_kv_restore(const ConversationKv& image, const QsaState& st, const ModelGeometry& g, int64_t upto,
                         bool index, strata::kv::Transfer& t, std::string& error) {
     if (!conversation_kv_validate(image, st, g, upto, index, error)) return false;
-    if (st.kv_mode != 0)
-        return fail(error, "restoring a streamed (kv_mode 1/2) layer needs the streamed-mode residency movers, "
-                           "which this build does not include");
     LayerExtent x;
     layer_extent(st, g, upto, index, x, error);
     const auto dst = layer_sources(st);
     const ConversationBuffer* src[5] = {&image.k, &image.v, &image.k_scale, &image.v_scale, &image.pooled};
-    for (int i = 0; i < 5; ++i)
-        if (src[i]->size()) t.restore(*src[i], 0, src[i]->size(), layer_stream(st, x, i, dst[(size_t) i]));
+    for (int i = 0; i < 5; ++i) {
+        if (!src[i]->size()) continue;
+        if (i < 4 && st.kv_mode != 0)
+            t.host_restore(*src[i], 0, src[i]->size(), static_cast<uint8_t*>(const_cast<void*>(dst[(size_t) i])));
+        else
+            t.restore(*src[i], 0, src[i]->size(), layer_stream(st, x, i, dst[(size_t) i]));
+    }
+    if (st.kv_mode == 1) {
+        // the VRAM slots still hold the outgoing conversation: evict every block, resolve refills from the host copy
+        const strata::kernels::KvStreamMap map = st.map;
+        t.after([map](std::string& err) {
+            if (skv::stream_reset(map, nullptr) == SKV_OK) return true;
+            err = std::string("conversation snapshot residency restore: ") + skv_last_error();
+            return false;
+        });
+    } else if (st.kv_mode == 2 && x.cells > 0) {
+        // the ring holds the last n_slots pages: refill them (page b -> slot b % n_slots) from the restored bytes
+        const int64_t end = x.cells / x.page_size, begin = std::max<int64_t>(0, end - st.n_slots);
+        const auto slots = layer_slots(st);
+        for (int i = 0; i < 4; ++i) {
+            if (!src[i]->size()) continue;
+            const uint64_t pb = src[i]->size() / (uint64_t) end;
+            for (int64_t b = begin; b < end;) {
+                const int64_t sl = b % st.n_slots, run = std::min<int64_t>(end - b, st.n_slots - sl);
+                // restore(src, from, to, dst) writes image byte `from` at dst.base + from: the base is shifted so
+                // that page b lands in slot b % n_slots
+                strata::kv::DeviceStream ring;
+                ring.base = reinterpret_cast<const void*>(reinterpret_cast<uintptr_t>(slots[(size_t) i]) +
+                                                          (uint64_t) sl * pb - (uint64_t) b * pb);
+                t.restore(*src[i], (uint64_t) b * pb, (uint64_t) (b + run) * pb, ring);
+                b += run;
+            }
+        }
+    }
     return true;
 }
 
@@ -219,7 +263,6 @@ bool conversation_kv_restore(const ConversationKv& image, const QsaState& st, co
 bool conversation_kv_verify(const ConversationKv& image, const QsaState& st, const ModelGeometry& g, int64_t upto,
                             bool index, uint64_t& fingerprint, std::string& error) {
     if (!conversation_kv_validate(image, st, g, upto, index, error)) return false;
-    if (st.kv_mode != 0) return fail(error, "read-back of a streamed (kv_mode 1/2) layer is not part of this build");
     LayerExtent x;
     layer_extent(st, g, upto, index, x, error);
     const auto src = layer_sources(st);
@@ -227,10 +270,42 @@ bool conversation_kv_verify(const ConversationKv& image, const QsaState& st, con
     std::array<ConversationBuffer, 5> back;
     strata::kv::Transfer t;
     for (int i = 0; i < 5; ++i) {
-        back[(size_t) i].resize(x.bytes[(size_t) i]);
-        if (x.bytes[(size_t) i]) t.save(layer_stream(st, x, i, src[(size_t) i]), 0, x.bytes[(size_t) i], back[(size_t) i]);
+        const size_t n = x.bytes[(size_t) i];
+        back[(size_t) i].resize(n);
+        if (!n) continue;
+        if (i < 4 && st.kv_mode != 0)   // the authoritative host copy
+            t.host_copy(static_cast<const uint8_t*>(src[(size_t) i]), 0, n, back[(size_t) i]);
+        else
+            t.save(layer_stream(st, x, i, src[(size_t) i]), 0, n, back[(size_t) i]);
+    }
+    // a ring also keeps its last n_slots pages resident: read the slot arrays back too
+    std::array<std::vector<uint8_t>, 4> ring;
+    const int64_t end = x.page_size ? x.cells / x.page_size : 0;
+    if (st.kv_mode == 2 && end > 0) {
+        const auto slots = layer_slots(st);
+        for (int i = 0; i < 4; ++i) {
+            if (!saved[i]->size()) continue;
+            const uint64_t pb = saved[i]->size() / (uint64_t) end;
+            ring[(size_t) i].resize((size_t) (pb * (uint64_t) st.n_slots));
+            strata::kv::DeviceStream d;
+            d.base = slots[(size_t) i];
+            t.save(d, 0, ring[(size_t) i].size(), ring[(size_t) i].data());
+        }
     }
     if (!t.run(error, "conversation snapshot read-back")) return false;
+    if (st.kv_mode == 2 && end > 0) {
+        const int64_t begin = std::max<int64_t>(0, end - st.n_slots);
+        for (int i = 0; i < 4; ++i) {
+            if (!saved[i]->size()) continue;
+            const uint64_t pb = saved[i]->size() / (uint64_t) end;
+            std::vector<uint8_t> page((size_t) pb);
+            for (int64_t b = begin; b < end; ++b) {
+                if (!saved[i]->read(page.data(), (size_t) ((uint64_t) b * pb), (size_t) pb) ||
+                    std::memcmp(page.data(), ring[(size_t) i].data() + (uint64_t) (b % st.n_slots) * pb, (size_t) pb))
+                    return fail(error, "restored K/V bytes differ");
+            }
+        }
+    }
     uint64_t hash = 1469598103934665603ull;
     for (int i = 0; i < 5; ++i) {
         if (!(back[(size_t) i] == *saved[i])) return fail(error, "restored K/V bytes differ");

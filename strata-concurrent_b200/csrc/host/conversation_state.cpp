@@ -474,18 +474,6 @@ ConversationRestore conversation_snapshot_restore(const SavedConversation& image
                                                   const ConversationStageSet& stages, const ModelGeometry& g,
                                                   const QsaState& draft, std::string& error) {
     if (!conversation_snapshot_validate(image, ss, stages, g, draft, error)) return ConversationRestore::invalid;
-    // a streamed layer cannot be mounted by this build: refuse before the first write anywhere
-    auto streamed = [](const QsaState& st) { return st.kv_mode != 0; };
-    bool any_streamed = streamed(draft);
-    for (size_t j = 0; j < owned_count(ss); ++j) any_streamed |= streamed(owned_layer(ss, j));
-    for (int64_t i = 0; i < stage_count(stages); ++i)
-        for (size_t j = 0; j < owned_count(*stages.stages[i].session); ++j)
-            any_streamed |= streamed(owned_layer(*stages.stages[i].session, j));
-    if (any_streamed) {
-        fail(error, "mounting streamed (kv_mode 1/2) layers needs the streamed-mode residency movers, which this "
-                    "build does not include");
-        return ConversationRestore::invalid;
-    }
     const int64_t upto = (int64_t) image.live.ids.size();
     {
         const DeviceScope on(stages.main_device);

@@ -26,7 +26,10 @@ bool layer_extent(const QsaState& st, const ModelGeometry& g, int64_t upto, bool
 bool layer_usable(const QsaState& st, const LayerExtent& x, int64_t upto, std::string& error);
 /// The authoritative source/target of each stream (device pools in mode 0, host pools otherwise).
 std::array<const void*, 5> layer_sources(const QsaState& st);
-/// Stream `i` of a layer as the copy kernels address it (paged through page_table for the K/V streams).
+/// The device-resident pools of each stream (a streamed or ring layer's VRAM slots).
+std::array<const void*, 5> layer_slots(const QsaState& st);
+/// Stream `i` of a layer as the copy kernels address it (paged through page_table for the K/V streams of a
+/// block-pool layer, identity otherwise).
 strata::kv::DeviceStream layer_stream(const QsaState& st, const LayerExtent& x, int i, const void* base);
 
 /// The 18-entry geometry key every image and payload carries.

@@ -103,6 +103,10 @@ void Transfer::host_copy(const uint8_t* src, uint64_t from, uint64_t to, strata:
     if (to > from) host_.push_back(HostCopy{src, from, to, &dst});
 }
 
+void Transfer::host_restore(const strata::core::ConversationBuffer& src, uint64_t from, uint64_t to, uint8_t* dst) {
+    if (to > from) host_back_.push_back(HostBack{&src, from, to, dst});
+}
+
 bool Transfer::run(std::string& error, const char* what) {
     const cudaStream_t stream = nullptr;   // the legacy stream: ordered after the caller's earlier device work
     bool saving = true;
@@ -112,6 +116,20 @@ bool Transfer::run(std::string& error, const char* what) {
             error = std::string(what) + ": internal: a transfer batch mixes saves and restores";
             return false;
         }
+    }
+    if ((!host_.empty() && !host_back_.empty()) || (!items_.empty() && !host_.empty() && !saving) ||
+        (!items_.empty() && !host_back_.empty() && saving)) {
+        error = std::string(what) + ": internal: a transfer batch mixes saves and restores";
+        return false;
+    }
+    for (const HostBack& h : host_back_) {
+        bool ok = true;
+        h.src->visit(h.from, h.to - h.from, [&](const uint8_t* p, size_t n, size_t at) {
+            ok = cuda_ok(cudaMemcpyAsync(h.dst + at, p, n, cudaMemcpyDefault, stream), error, what,
+                         "host pool copy");
+            return ok;
+        });
+        if (!ok) return false;
     }
     for (const HostCopy& h : host_) {
         bool ok = true;
@@ -213,6 +231,8 @@ bool Transfer::run(std::string& error, const char* what) {
         }
         launched = true;
     }
+    for (auto& fn : after_)
+        if (!fn(error)) return false;
     if (!cuda_ok(cudaStreamSynchronize(stream), error, what, "synchronize")) return false;
     if (launched) {   // the status word the kernels of this batch reported into
         int dev = -1;
@@ -232,6 +252,8 @@ bool Transfer::run(std::string& error, const char* what) {
     }
     items_.clear();
     host_.clear();
+    host_back_.clear();
+    after_.clear();
     return true;
 }
 

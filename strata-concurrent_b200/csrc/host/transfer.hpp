@@ -12,6 +12,7 @@
 #include "strata_kv/conversation_buffer.hpp"
 
 #include <cstdint>
+#include <functional>
 #include <string>
 #include <vector>
 
@@ -37,8 +38,13 @@ public:
     void restore(const uint8_t* src, uint64_t from, uint64_t to, const DeviceStream& dst);
     /// Host -> host copy run in the same batch (a streamed layer's authoritative host pool).
     void host_copy(const uint8_t* src, uint64_t from, uint64_t to, strata::core::ConversationBuffer& dst);
+    /// The reverse: bytes [from, to) of `src` -> the same offsets of host memory `dst`.
+    void host_restore(const strata::core::ConversationBuffer& src, uint64_t from, uint64_t to, uint8_t* dst);
+    /// Work to enqueue on the batch's stream after every copy of it (a residency reset that must follow the
+    /// writes); returns false with `error` set to refuse.
+    void after(std::function<bool(std::string& error)> fn) { after_.push_back(std::move(fn)); }
 
-    bool empty() const { return items_.empty() && host_.empty(); }
+    bool empty() const { return items_.empty() && host_.empty() && host_back_.empty() && after_.empty(); }
     size_t items() const { return items_.size(); }
 
     /// Run everything queued (saves and restores may not be mixed in one batch).  On failure `error` names the
@@ -62,8 +68,15 @@ private:
         uint64_t from, to;
         strata::core::ConversationBuffer* dst;
     };
+    struct HostBack {
+        const strata::core::ConversationBuffer* src;
+        uint64_t from, to;
+        uint8_t* dst;
+    };
     std::vector<Item> items_;
     std::vector<HostCopy> host_;
+    std::vector<HostBack> host_back_;
+    std::vector<std::function<bool(std::string&)>> after_;
 };
 
 /// Bytes of the per-device staging image currently held (for tests and telemetry).

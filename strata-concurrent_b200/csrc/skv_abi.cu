@@ -167,6 +167,32 @@ struct skv_pool {
     std::mutex mu;
 };
 
+namespace skv {
+namespace {
+std::mutex g_pools_mu;
+std::vector<const skv_pool*> g_pools;   // every live pool, created or wrapped
+
+void register_pool(const skv_pool* p) {
+    std::lock_guard<std::mutex> lock(g_pools_mu);
+    g_pools.push_back(p);
+}
+void unregister_pool(const skv_pool* p) {
+    std::lock_guard<std::mutex> lock(g_pools_mu);
+    g_pools.erase(std::remove(g_pools.begin(), g_pools.end(), p), g_pools.end());
+}
+}  // namespace
+
+bool in_block_pool(const void* address) {
+    const auto a = reinterpret_cast<uintptr_t>(address);
+    std::lock_guard<std::mutex> lock(g_pools_mu);
+    for (const skv_pool* p : g_pools) {
+        const auto b = reinterpret_cast<uintptr_t>(p->base);
+        if (a >= b && a - b < (uint64_t) p->n_blocks * p->block_bytes) return true;
+    }
+    return false;
+}
+}  // namespace skv
+
 extern "C" {
 
 const char* skv_last_error(void) { return t_error.c_str(); }
@@ -196,6 +222,7 @@ int skv_pool_create(int device, int64_t n_blocks, uint64_t block_bytes, skv_pool
     pool->free_list.resize((size_t) n_blocks);
     for (int64_t i = 0; i < n_blocks; ++i) pool->free_list[(size_t) i] = (int32_t) (n_blocks - 1 - i);
     pool->used.assign((size_t) n_blocks, 0);
+    register_pool(pool.get());
     *out = pool.release();
     return SKV_OK;
 }
@@ -215,12 +242,14 @@ int skv_pool_wrap(int device, void* base, int64_t n_blocks, uint64_t block_bytes
     pool->free_list.resize((size_t) n_blocks);
     for (int64_t i = 0; i < n_blocks; ++i) pool->free_list[(size_t) i] = (int32_t) (n_blocks - 1 - i);
     pool->used.assign((size_t) n_blocks, 0);
+    register_pool(pool.get());
     *out = pool.release();
     return SKV_OK;
 }
 
 int skv_pool_destroy(skv_pool* pool) {
     if (!pool) return SKV_OK;
+    unregister_pool(pool);
     if (!pool->owned) {
         delete pool;
         return SKV_OK;

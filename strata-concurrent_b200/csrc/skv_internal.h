@@ -84,6 +84,10 @@ struct ChainArgs {
 /// Returns the context of the CURRENT device, creating it on first use.  Null on failure (error set).
 DeviceCtx* current_ctx();
 
+/// True when `address` lies inside a live block pool (skv_pool_create / skv_pool_wrap): such a resident layer is
+/// addressed through its page table; any other resident layer is identity-addressed.
+bool in_block_pool(const void* address);
+
 /// Thread-local error message used by skv_last_error().
 void set_error(const std::string& message);
 int fail(int code, const std::string& message);

@@ -4,6 +4,12 @@ snapshot_gpu_test parks config 1 (full geometry, 4,096 tokens, seed 1) from a po
 conversation_snapshot_save, and the SR4H payload of the parked image must hash to the FNV-1a the reference's own
 save + encode produced from its identity pool (tests/golden/golden.json).  It then mounts the image into a
 differently permuted pool and reads every byte back; see the program's header for the full list.
+
+kv_stream_gpu_test checks the block movers of streamed and ring layers (reset, the CLOCK resolve against the
+oracle's sequential restatement, ring table / restore, stage from host).
+
+The reference's own GPU test program, conversation_snapshot_test (built unchanged against this build by
+oracle/Makefile), parks and mounts every KV format in resident, streamed and ring layers, whole and layer-split.
 """
 import json
 import os
@@ -42,3 +48,21 @@ def test_snapshot_park_mount_matches_reference_payload(torch_cuda):
     print(r.stdout)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
     assert "checks passed" in r.stdout
+
+
+def test_kv_stream_block_movers_match_the_oracle(torch_cuda):
+    exe = build("kv_stream_gpu_test")
+    r = subprocess.run([exe], capture_output=True, text=True, timeout=600)
+    print(r.stdout)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
+    assert "checks passed" in r.stdout
+
+
+def test_reference_gpu_snapshot_suite_passes_against_the_drop_in(torch_cuda):
+    exe = os.path.join(ORACLE, "_ref", "ref_conversation_snapshot_test")
+    if not os.path.exists(exe):
+        pytest.skip("ref_conversation_snapshot_test not built (the reference tree was not present at build time)")
+    r = subprocess.run([exe], capture_output=True, text=True, timeout=600)
+    print(r.stdout)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
+    assert "conversation_snapshot_test:" in r.stdout and "checks passed" in r.stdout
