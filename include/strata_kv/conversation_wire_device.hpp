@@ -11,7 +11,9 @@
 //
 // Destination: host memory (pinned for full PCIe speed; the pool goes down as one device-to-host copy per run of
 // blobs that share a device), or device memory on the device that holds every device-resident blob (for a
-// payload that then moves over NVLink or CUDA IPC as one contiguous buffer).
+// payload that then moves over NVLink or CUDA IPC as one contiguous buffer).  The mount side,
+// conversation_wire_mount_device, takes such a device payload (a peer's, through CUDA IPC) straight into the
+// decode session's pools.
 #pragma once
 
 #include "strata_kv/conversation_snapshot.hpp"
@@ -47,5 +49,24 @@ bool conversation_wire_pack_device(const ConversationView& view, const SessionSt
                                    const QsaState& draft, const WireIdentity& identity, uint8_t* dst,
                                    uint64_t capacity, WirePlan& plan, WireEncoded& out, std::string& error,
                                    const WireDeviceOptions& options = {});
+
+/// Mounts a session straight from an SR4H payload that lies in DEVICE memory - this device's, or a peer GPU's
+/// mapped through CUDA IPC (the prefill instance's packed payload on the same node).  The header and records are
+/// copied to the host and decoded with every check of conversation_wire_decode except the payload hash (the blobs
+/// are never read by the host); the whole image is validated against the session exactly as
+/// conversation_snapshot_restore validates it; then every blob goes from the payload to its place - K/V through
+/// the destination layer's table, the running state, the draft, the layer-split stages - by the copy kernels
+/// (NVLink loads for a peer payload), with the streamed / ring residency fix-ups of a mount.  `meta` receives the
+/// image's metadata and its retained checkpoints (host copies); its K/V buffers and live running state stay empty,
+/// because their bytes went to the device.  Returns invalid (nothing written) or transfer_failed like
+/// conversation_snapshot_restore.
+ConversationRestore conversation_wire_mount_device(const uint8_t* payload, uint64_t bytes, SessionState& session,
+                                                   const ConversationStageSet& stages, const ModelGeometry& g,
+                                                   const QsaState& draft, const WireExpect& expect,
+                                                   SavedConversation& meta, WireDecoded& info, std::string& error);
+ConversationRestore conversation_wire_mount_device(const uint8_t* payload, uint64_t bytes, SessionState& session,
+                                                   const ModelGeometry& g, const QsaState& draft,
+                                                   const WireExpect& expect, SavedConversation& meta,
+                                                   WireDecoded& info, std::string& error);
 
 }  // namespace strata::core

@@ -238,6 +238,11 @@ bool conversation_kv_save(ConversationKv& image, const QsaState& st, const Model
 
 bool conversation_kv_validate(const ConversationKv& image, const QsaState& st, const ModelGeometry& g, int64_t upto,
                               bool index, std::string& error) {
+    return kv_validate_sized(image, st, g, upto, index, error, own_size);
+}
+
+bool snapshot_detail::kv_validate_sized(const ConversationKv& image, const QsaState& st, const ModelGeometry& g,
+                                        int64_t upto, bool index, std::string& error, const SizeOf& size_of) {
     LayerExtent x;
     if (!layer_extent(st, g, upto, index, x, error) || !layer_usable(st, x, upto, error)) return false;
     if (image.format != x.format || image.cells != x.cells || image.heads != g.n_head_kv ||
@@ -246,7 +251,7 @@ bool conversation_kv_validate(const ConversationKv& image, const QsaState& st, c
         return fail(error, "incompatible K/V geometry");
     const ConversationBuffer* b[5] = {&image.k, &image.v, &image.k_scale, &image.v_scale, &image.pooled};
     for (int i = 0; i < 5; ++i)
-        if (b[i]->size() != x.bytes[(size_t) i]) return fail(error, "invalid K/V payload size");
+        if (size_of(b[i], b[i]->size()) != x.bytes[(size_t) i]) return fail(error, "invalid K/V payload size");
     const auto dst = layer_sources(st);
     for (int i = 0; i < 5; ++i)
         if (x.bytes[(size_t) i] && !dst[(size_t) i]) return fail(error, "missing target state buffer");

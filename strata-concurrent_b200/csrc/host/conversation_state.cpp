@@ -258,12 +258,17 @@ bool conversation_session_sizes(const ModelGeometry& g, const SessionState& ss, 
 
 bool conversation_checkpoint_validate(const ConversationCheckpoint& c, const SessionState& ss, const ModelGeometry& g,
                                       std::string& error) {
+    return checkpoint_validate_sized(c, ss, g, error, own_size);
+}
+
+bool snapshot_detail::checkpoint_validate_sized(const ConversationCheckpoint& c, const SessionState& ss,
+                                                const ModelGeometry& g, std::string& error, const SizeOf& size_of) {
     ConversationStateSizes z;
     if (!running_targets(ss, g, c.ids.size(), z, error)) return false;
     const size_t layers = owned_count(ss);
-    if (c.gdn.size() != z.gdn || c.ple.size() != (ss.ple_hist ? z.ple : 0) || c.tails.size() != layers * z.tail ||
-        c.dead.size() != layers * z.dead || c.block_pos.size() != layers * z.block_pos ||
-        !images_ordered(c.imgs, c.ids.size()))
+    auto n = [&](const std::vector<uint8_t>& v) { return size_of(&v, v.size()); };
+    if (n(c.gdn) != z.gdn || n(c.ple) != (ss.ple_hist ? z.ple : 0) || n(c.tails) != layers * z.tail ||
+        n(c.dead) != layers * z.dead || n(c.block_pos) != layers * z.block_pos || !images_ordered(c.imgs, c.ids.size()))
         return fail(error, "invalid checkpoint running-state payload");
     return true;
 }
@@ -432,6 +437,12 @@ bool conversation_snapshot_save(SavedConversation& image, const ConversationView
 bool conversation_snapshot_validate(const SavedConversation& image, const SessionState& ss,
                                     const ConversationStageSet& stages, const ModelGeometry& g, const QsaState& draft,
                                     std::string& error) {
+    return snapshot_validate_sized(image, ss, stages, g, draft, error, own_size);
+}
+
+bool snapshot_detail::snapshot_validate_sized(const SavedConversation& image, const SessionState& ss,
+                                              const ConversationStageSet& stages, const ModelGeometry& g,
+                                              const QsaState& draft, std::string& error, const SizeOf& size_of) {
     if (!stages_tile(stages, ss, g, error)) return false;
     if (!image.live.stage_parts.empty()) return fail(error, "layer-split parking is not supported");
     if ((int64_t) image.stage_parts.size() != stage_count(stages))
@@ -441,13 +452,14 @@ bool conversation_snapshot_validate(const SavedConversation& image, const Sessio
     if (image.layer_lo != ss.layer_lo || image.layer_hi != ss.layer_hi)
         return fail(error, "snapshot from another session layer range");
     const ConversationView view{image.live.ids, image.live.imgs, image.checkpoints, image.cvec};
-    if (!view_ok(view, ss, stages, g, error) || !conversation_checkpoint_validate(image.live, ss, g, error)) return false;
+    if (!view_ok(view, ss, stages, g, error) || !checkpoint_validate_sized(image.live, ss, g, error, size_of))
+        return false;
     const size_t layers = owned_count(ss);
     if (image.kv.size() != layers + 1) return fail(error, "invalid K/V layer count");
     const int64_t upto = (int64_t) image.live.ids.size();
     for (size_t j = 0; j < layers; ++j)
-        if (!conversation_kv_validate(image.kv[j], owned_layer(ss, j), g, upto, true, error)) return false;
-    if (!conversation_kv_validate(image.kv.back(), draft, g, upto, false, error)) return false;
+        if (!kv_validate_sized(image.kv[j], owned_layer(ss, j), g, upto, true, error, size_of)) return false;
+    if (!kv_validate_sized(image.kv.back(), draft, g, upto, false, error, size_of)) return false;
     for (size_t i = 0; i < image.stage_parts.size(); ++i) {
         const ConversationStageSnapshot& part = image.stage_parts[i];
         const SessionState& sss = *stages.stages[i].session;
@@ -457,10 +469,10 @@ bool conversation_snapshot_validate(const SavedConversation& image, const Sessio
             part.state.ids.size() != image.live.ids.size() ||
             !std::equal(part.state.ids.begin(), part.state.ids.end(), image.live.ids.begin()))
             return fail(error, "layer-split stage part is not a live token prefix");
-        if (!conversation_checkpoint_validate(part.state, sss, g, error)) return false;
+        if (!checkpoint_validate_sized(part.state, sss, g, error, size_of)) return false;
         if (part.kv.size() != owned_count(sss)) return fail(error, "invalid layer-split stage K/V layer count");
         for (size_t j = 0; j < part.kv.size(); ++j)
-            if (!conversation_kv_validate(part.kv[j], owned_layer(sss, j), g, upto, true, error)) return false;
+            if (!kv_validate_sized(part.kv[j], owned_layer(sss, j), g, upto, true, error, size_of)) return false;
     }
     return true;
 }

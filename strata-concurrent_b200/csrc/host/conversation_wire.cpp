@@ -550,8 +550,12 @@ bool header_self_check(const WireHeaderRecord& h, std::string& error) {
 
 class Decoder {
 public:
-    Decoder(const WireSource& src, const WireExpect& expect, std::string& error)
-        : src_(src), expect_(expect), error_(error) {}
+    /// `shape` null: a full decode (blobs copied into a fresh image that replaces the caller's on success).
+    /// `shape` set: a shape decode - the image is built in place with every blob left empty and recorded in
+    /// `shape` (key -> payload offset and size); no blob byte and no hash is read from the source.
+    Decoder(const WireSource& src, const WireExpect& expect, std::string& error,
+            wire_detail::BlobTable* shape = nullptr)
+        : src_(src), expect_(expect), error_(error), shape_(shape) {}
 
     bool run(SavedConversation& image, WireDecoded& info) {
         if (src_.size() < kWireHeaderRecordBytes)
@@ -585,7 +589,13 @@ public:
                 return refuse(error_, "pack_hash " + hex16(h_.pack_hash) + " differs from the expected " +
                                           hex16(expect_.pack_hash));
         }
-        if (!hash_payload()) return false;
+        if (shape_) {
+            if (expect_.check_payload_hash)
+                return refuse(error_, "a shape decode never reads the blobs, so it cannot check the payload hash");
+            hash_ = 0;
+        } else if (!hash_payload()) {
+            return false;
+        }
         if (expect_.check_payload_hash && hash_ != expect_.payload_hash)
             return refuse(error_, "payload hash " + hex16(hash_) + " differs from the expected " +
                                       hex16(expect_.payload_hash));
@@ -625,8 +635,13 @@ public:
         if (pool_bytes_ != (blobs_ ? align64(cursor_) : 0))
             return refuse(error_, "the blob pool's size disagrees with the blobs it holds");
 
-        // every check passed: build the image
-        SavedConversation out;
+        // every check passed: build the image (a shape decode builds in place, so the recorded keys stay valid)
+        SavedConversation local;
+        SavedConversation& out = shape_ ? image : local;
+        if (shape_) {
+            out = SavedConversation{};
+            shape_->clear();
+        }
         for (int i = 0; i < 18; ++i) out.geometry[(size_t) i] = (int64_t) h_.geometry[i];
         out.layer_lo = (int64_t) h_.layer_lo;
         out.layer_hi = (int64_t) h_.layer_hi;
@@ -649,7 +664,7 @@ public:
             for (size_t j = 0; j < s.kv.size(); ++j)
                 if (!make_kv(stages[i].kv[j], s.kv[j])) return false;
         }
-        image = std::move(out);
+        if (!shape_) image = std::move(out);
         info = WireDecoded{};
         info.bytes = h_.payload_bytes;
         info.payload_hash = hash_;
@@ -840,12 +855,20 @@ private:
         return true;
     }
     bool make_buffer(const Ref& r, ConversationBuffer& b) {
+        if (shape_) {
+            if (r.bytes) (*shape_)[&b] = wire_detail::BlobAt{r.off, r.bytes};
+            return true;
+        }
         b.resize((size_t) r.bytes);
         bool ok = true;
         b.visit(0, (size_t) r.bytes, [&](uint8_t* p, size_t n, size_t at) { return ok = copy_out(r, p, n, at); });
         return ok;
     }
     bool make_vec(const Ref& r, std::vector<uint8_t>& v) {
+        if (shape_) {
+            if (r.bytes) (*shape_)[&v] = wire_detail::BlobAt{r.off, r.bytes};
+            return true;
+        }
         v.resize((size_t) r.bytes);
         return copy_out(r, v.data(), v.size(), 0);
     }
@@ -878,6 +901,7 @@ private:
     const WireSource& src_;
     const WireExpect& expect_;
     std::string& error_;
+    wire_detail::BlobTable* shape_ = nullptr;
     WireHeaderRecord h_{};
     uint64_t pool_off_ = 0, pool_bytes_ = 0, cursor_ = 0, hash_ = 0;
     size_t blobs_ = 0;
@@ -890,6 +914,14 @@ bool conversation_wire_decode(const WireSource& source, SavedConversation& image
     Decoder d(source, expect, error);
     return d.run(image, info);
 }
+
+namespace wire_detail {
+bool decode_shape(const WireSource& source, SavedConversation& image, WireDecoded& info, const WireExpect& expect,
+                  BlobTable& blobs, std::string& error) {
+    Decoder d(source, expect, error, &blobs);
+    return d.run(image, info);
+}
+}  // namespace wire_detail
 
 bool conversation_wire_decode(const uint8_t* data, uint64_t bytes, SavedConversation& image, WireDecoded& info,
                               const WireExpect& expect, std::string& error) {

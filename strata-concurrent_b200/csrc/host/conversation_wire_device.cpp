@@ -13,6 +13,7 @@
 //    engine, and every byte of the pool nobody wrote is zeroed.
 #include "strata_kv/conversation_wire_device.hpp"
 
+#include "kv_stream_detail.h"
 #include "snapshot_detail.hpp"
 #include "strata_kv.h"
 #include "wire_detail.hpp"
@@ -21,6 +22,7 @@
 
 #include <algorithm>
 #include <cstring>
+#include <functional>
 #include <map>
 #include <unordered_map>
 
@@ -46,7 +48,7 @@ struct Source {
 using Side = std::unordered_map<const void*, Source>;
 
 bool pfail(std::string& error, const std::string& why) {
-    error = "conversation wire device pack: " + why;
+    error = "conversation wire device: " + why;
     return false;
 }
 bool cuda_ok(cudaError_t e, std::string& error, const char* step) {
@@ -406,6 +408,265 @@ bool conversation_wire_pack_device(const ConversationView& view, const SessionSt
                                    uint64_t capacity, WirePlan& plan, WireEncoded& out, std::string& error,
                                    const WireDeviceOptions& opt) {
     return conversation_wire_pack_device(view, ss, {}, g, draft, identity, dst, capacity, plan, out, error, opt);
+}
+
+// ------------------------------------------------------------------------------------------------ device mount
+
+namespace {
+
+/// The records of a device payload, served from a host copy of [0, blob_pool_off); size() is the whole payload's.
+class RecordSource final : public WireSource {
+public:
+    RecordSource(std::vector<uint8_t> records, uint64_t total) : rec_(std::move(records)), total_(total) {}
+    uint64_t size() const override { return total_; }
+    bool read(uint8_t* dst, uint64_t offset, size_t bytes) const override {
+        if (offset > rec_.size() || bytes > rec_.size() - offset) return false;
+        std::memcpy(dst, rec_.data() + offset, bytes);
+        return true;
+    }
+    const uint8_t* span(uint64_t offset, size_t bytes) const override {
+        if (offset > rec_.size() || bytes > rec_.size() - offset) return nullptr;
+        return rec_.data() + offset;
+    }
+
+private:
+    std::vector<uint8_t> rec_;
+    uint64_t total_;
+};
+
+/// One device's share of a mount: copy-kernel segments by engine, plain copies for what the kernels cannot take,
+/// and work that must follow the writes.
+struct MountBatch {
+    std::vector<skv_segment> tma, vec;
+    struct Plain {
+        void* dst;
+        const void* src;
+        uint64_t bytes;
+    };
+    std::vector<Plain> plain;
+    std::vector<std::function<bool(std::string&)>> after;
+
+    /// src (device payload) -> dst through `d` (paged or contiguous).
+    void add(const uint8_t* src, const strata::kv::DeviceStream& d, uint64_t from, uint64_t bytes) {
+        if (!bytes) return;
+        skv_segment sg{};
+        sg.src = src;
+        sg.bytes = bytes;
+        if (d.pages) {
+            sg.dst = const_cast<void*>(d.base);
+            sg.dst_pages = d.pages + from / d.page_bytes;
+            sg.page_bytes = d.page_bytes;
+            sg.dst_page_limit = d.page_limit;
+            (d.page_bytes >= 1024 && d.page_bytes <= 16384 ? tma : vec).push_back(sg);
+            return;
+        }
+        uint8_t* dst = const_cast<uint8_t*>(static_cast<const uint8_t*>(d.base)) + from;
+        if (((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst) | bytes) & 15u) == 0) {
+            sg.dst = dst;
+            tma.push_back(sg);
+        } else {
+            plain.push_back(Plain{dst, src, bytes});
+        }
+    }
+    void add_plain(void* dst, const void* src, uint64_t bytes) {
+        if (bytes) plain.push_back(Plain{dst, src, bytes});
+    }
+
+    bool run(int device, std::string& error) {
+        const DeviceScope on(device);
+        int dev = 0;
+        if (!cuda_ok(cudaGetDevice(&dev), error, "cudaGetDevice")) return false;
+        if (skv_clear_status(dev, nullptr) != SKV_OK) return pfail(error, skv_last_error());
+        for (auto* list : {&tma, &vec}) {
+            const int engine = list == &tma ? SKV_COPY_TMA : SKV_COPY_VEC;
+            for (size_t i = 0; i < list->size(); i += SKV_COPY_MAX_SEGMENTS) {
+                const int n = (int) std::min<size_t>(SKV_COPY_MAX_SEGMENTS, list->size() - i);
+                if (skv_copy(list->data() + i, n, engine, nullptr) != SKV_OK)
+                    return pfail(error, std::string("mount copy: ") + skv_last_error());
+            }
+        }
+        for (const Plain& p : plain)
+            if (!cuda_ok(cudaMemcpyAsync(p.dst, p.src, p.bytes, cudaMemcpyDefault, nullptr), error, "mount copy"))
+                return false;
+        for (auto& fn : after)
+            if (!fn(error)) return false;
+        if (!cuda_ok(cudaStreamSynchronize(nullptr), error, "synchronize")) return false;
+        return status_clean(dev, error);
+    }
+};
+
+/// One layer's K/V from the payload into `st` (validated already): the mount twin of enqueue_kv_restore.
+void mount_kv(const ConversationKv& k, const uint8_t* payload, const wire_detail::BlobTable& blobs,
+              const QsaState& st, const ModelGeometry& g, int64_t upto, bool index, MountBatch& b) {
+    LayerExtent x;
+    std::string ignored;
+    layer_extent(st, g, upto, index, x, ignored);
+    const auto dst = layer_sources(st);
+    const ConversationBuffer* bufs[5] = {&k.k, &k.v, &k.k_scale, &k.v_scale, &k.pooled};
+    std::array<const uint8_t*, 5> src{};
+    for (int i = 0; i < 5; ++i) {
+        const auto it = blobs.find(bufs[i]);
+        if (it == blobs.end()) continue;
+        src[(size_t) i] = payload + it->second.off;
+        if (i < 4 && st.kv_mode != 0)   // the authoritative host copy
+            b.add_plain(const_cast<void*>(dst[(size_t) i]), src[(size_t) i], it->second.bytes);
+        else
+            b.add(src[(size_t) i], layer_stream(st, x, i, dst[(size_t) i]), 0, it->second.bytes);
+    }
+    if (st.kv_mode == 1) {
+        const strata::kernels::KvStreamMap map = st.map;
+        b.after.push_back([map](std::string& err) {
+            if (skv::stream_reset(map, nullptr) == SKV_OK) return true;
+            err = std::string("conversation wire device mount: residency reset: ") + skv_last_error();
+            return false;
+        });
+    } else if (st.kv_mode == 2 && x.cells > 0) {
+        const int64_t end = x.cells / x.page_size, begin = std::max<int64_t>(0, end - st.n_slots);
+        const auto slots = layer_slots(st);
+        for (int i = 0; i < 4; ++i) {
+            const auto it = blobs.find(bufs[i]);
+            if (it == blobs.end()) continue;
+            const uint64_t pb = it->second.bytes / (uint64_t) end;
+            for (int64_t p = begin; p < end;) {
+                const int64_t sl = p % st.n_slots, run = std::min<int64_t>(end - p, st.n_slots - sl);
+                strata::kv::DeviceStream ring;
+                ring.base = static_cast<const uint8_t*>(slots[(size_t) i]) + (uint64_t) sl * pb;
+                b.add(src[(size_t) i] + (uint64_t) p * pb, ring, 0, (uint64_t) run * pb);
+                p += run;
+            }
+        }
+    }
+}
+
+/// A checkpoint's running state from the payload into `ss` (validated already): the mount twin of
+/// conversation_checkpoint_restore, including the indexer's spare row.
+void mount_running(const ConversationCheckpoint& c, const uint8_t* payload, const wire_detail::BlobTable& blobs,
+                   const SessionState& ss, const ModelGeometry& g, MountBatch& b) {
+    ConversationStateSizes z;
+    std::string ignored;
+    conversation_session_sizes(g, ss, z, ignored);
+    auto at = [&](const std::vector<uint8_t>& v) -> const uint8_t* {
+        const auto it = blobs.find(&v);
+        return it == blobs.end() ? nullptr : payload + it->second.off;
+    };
+    auto flat = [](const void* p) {
+        strata::kv::DeviceStream s;
+        s.base = p;
+        return s;
+    };
+    if (const uint8_t* p = at(c.gdn)) b.add(p, flat(ss.gdn_state), 0, z.gdn);
+    if (const uint8_t* p = at(c.ple)) b.add(p, flat(ss.ple_hist), 0, z.ple);
+    const uint8_t *tails = at(c.tails), *dead = at(c.dead), *pos = at(c.block_pos);
+    const uint64_t block = (uint64_t) strata::kernels::qsa_real_shapes().idx_block;
+    for (size_t j = 0; j < owned_count(ss); ++j) {
+        const QsaState& st = owned_layer(ss, j);
+        if (tails) b.add(tails + j * z.tail, flat(st.idx_tail), 0, z.tail);
+        if (dead) b.add(dead + j * z.dead, flat(st.idx_dead), 0, z.dead);
+        if (pos) b.add_plain(st.idx_block_pos, pos + j * z.block_pos, z.block_pos);
+        if (dead && !c.ids.empty())   // the indexer's moving spare row is the dead key again
+            b.add(dead + j * z.dead, flat(st.idx_pooled + (c.ids.size() / block) * (size_t) g.idx_key_dim), 0, z.dead);
+    }
+}
+
+/// Retained checkpoints live on the host (the cache keeps them): copy their blobs out of the payload.
+bool fill_retained(ConversationCheckpoint& c, const uint8_t* payload, wire_detail::BlobTable& blobs,
+                   std::string& error) {
+    for (std::vector<uint8_t>* v : {&c.gdn, &c.ple, &c.tails, &c.dead, &c.block_pos}) {
+        const auto it = blobs.find(v);
+        if (it == blobs.end()) continue;
+        v->resize((size_t) it->second.bytes);
+        if (!cuda_ok(cudaMemcpy(v->data(), payload + it->second.off, v->size(), cudaMemcpyDefault), error,
+                     "retained checkpoint copy"))
+            return false;
+        blobs.erase(it);
+    }
+    for (auto& part : c.stage_parts)
+        if (!fill_retained(part, payload, blobs, error)) return false;
+    return true;
+}
+
+}  // namespace
+
+ConversationRestore conversation_wire_mount_device(const uint8_t* payload, uint64_t bytes, SessionState& ss,
+                                                   const ConversationStageSet& stages, const ModelGeometry& g,
+                                                   const QsaState& draft, const WireExpect& expect,
+                                                   SavedConversation& meta, WireDecoded& info, std::string& error) {
+    using R = ConversationRestore;
+    if (!payload || bytes < kWireHeaderRecordBytes) {
+        pfail(error, "no payload, or one shorter than its header");
+        return R::invalid;
+    }
+    std::vector<uint8_t> head(kWireHeaderRecordBytes);
+    if (!cuda_ok(cudaMemcpy(head.data(), payload, head.size(), cudaMemcpyDefault), error, "header copy")) return R::invalid;
+    WireHeaderRecord h{};
+    if (!conversation_wire_peek(head.data(), head.size(), h, error)) return R::invalid;
+    if (h.blob_pool_off < kWireHeaderRecordBytes || h.blob_pool_off > bytes || h.payload_bytes > bytes) {
+        pfail(error, "the header's records or payload run past the " + std::to_string(bytes) + " device bytes");
+        return R::invalid;
+    }
+    std::vector<uint8_t> records((size_t) h.blob_pool_off);
+    if (!cuda_ok(cudaMemcpy(records.data(), payload, records.size(), cudaMemcpyDefault), error, "records copy"))
+        return R::invalid;
+    RecordSource src(std::move(records), bytes);
+    wire_detail::BlobTable blobs;
+    if (!wire_detail::decode_shape(src, meta, info, expect, blobs, error)) return R::invalid;
+    for (auto& c : meta.checkpoints)
+        if (!fill_retained(c, payload, blobs, error)) return R::invalid;
+    const wire_detail::BlobTable& table = blobs;
+    const SizeOf sizes = [&table](const void* key, uint64_t real) -> uint64_t {
+        const auto it = table.find(key);
+        return it == table.end() ? real : it->second.bytes;
+    };
+    if (!snapshot_validate_sized(meta, ss, stages, g, draft, error, sizes)) return R::invalid;
+
+    // every check passed: the writes
+    const int64_t upto = (int64_t) meta.live.ids.size();
+    const int main_dev = resolve(stages.main_device);
+    const int draft_dev = stages.empty() ? main_dev : resolve(stages.draft_device);
+    {
+        const DeviceScope on(main_dev);
+        if (!device_sync(error)) return R::transfer_failed;
+        MountBatch b;
+        for (size_t j = 0; j < owned_count(ss); ++j) mount_kv(meta.kv[j], payload, blobs, owned_layer(ss, j), g, upto, true, b);
+        mount_running(meta.live, payload, blobs, ss, g, b);
+        if (!b.run(main_dev, error)) return R::transfer_failed;
+    }
+    {
+        MountBatch b;
+        mount_kv(meta.kv.back(), payload, blobs, draft, g, upto, false, b);
+        if (draft_dev != main_dev) {
+            const DeviceScope on(draft_dev);
+            if (!device_sync(error)) return R::transfer_failed;
+        }
+        if (!b.run(draft_dev, error)) return R::transfer_failed;
+    }
+    const size_t n = meta.live.ids.size();
+    ss.ple_prev[0] = n >= 2 ? meta.live.ids[n - 2] : -1;
+    ss.ple_prev[1] = n >= 1 ? meta.live.ids[n - 1] : -1;
+    for (size_t i = 0; i < meta.stage_parts.size(); ++i) {
+        const ConversationStage& stage = stages.stages[i];
+        const ConversationStageSnapshot& part = meta.stage_parts[i];
+        const int dev = resolve(stage.device);
+        {
+            const DeviceScope on(dev);
+            if (!device_sync(error)) return R::transfer_failed;
+        }
+        MountBatch b;
+        for (size_t j = 0; j < part.kv.size(); ++j)
+            mount_kv(part.kv[j], payload, blobs, owned_layer(*stage.session, j), g, upto, true, b);
+        mount_running(part.state, payload, blobs, *stage.session, g, b);
+        if (!b.run(dev, error)) return R::transfer_failed;
+        stage.session->ple_prev[0] = n >= 2 ? meta.live.ids[n - 2] : -1;
+        stage.session->ple_prev[1] = n >= 1 ? meta.live.ids[n - 1] : -1;
+    }
+    return R::restored;
+}
+
+ConversationRestore conversation_wire_mount_device(const uint8_t* payload, uint64_t bytes, SessionState& ss,
+                                                   const ModelGeometry& g, const QsaState& draft,
+                                                   const WireExpect& expect, SavedConversation& meta,
+                                                   WireDecoded& info, std::string& error) {
+    return conversation_wire_mount_device(payload, bytes, ss, {}, g, draft, expect, meta, info, error);
 }
 
 }  // namespace strata::core

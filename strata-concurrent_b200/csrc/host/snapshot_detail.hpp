@@ -5,6 +5,7 @@
 #include "transfer.hpp"
 
 #include <array>
+#include <functional>
 #include <initializer_list>
 #include <string>
 
@@ -57,6 +58,17 @@ bool stages_tile(const ConversationStageSet& stages, const SessionState& main_ss
 /// The live branch and every retained checkpoint are consistent prefixes of it.
 bool view_ok(const ConversationView& view, const SessionState& ss, const ConversationStageSet& stages,
              const ModelGeometry& g, std::string& error);
+
+/// The byte count validation sees for a buffer or vector of an image: its own size(), or a side table's for a
+/// shape image whose bytes live elsewhere (a device payload).  key = the ConversationBuffer / std::vector.
+using SizeOf = std::function<uint64_t(const void* key, uint64_t real)>;
+inline uint64_t own_size(const void*, uint64_t real) { return real; }
+bool kv_validate_sized(const ConversationKv& image, const QsaState& st, const ModelGeometry& g, int64_t upto,
+                       bool index, std::string& error, const SizeOf& size_of);
+bool checkpoint_validate_sized(const ConversationCheckpoint& c, const SessionState& ss, const ModelGeometry& g,
+                               std::string& error, const SizeOf& size_of);
+bool snapshot_validate_sized(const SavedConversation& image, const SessionState& ss, const ConversationStageSet& stages,
+                             const ModelGeometry& g, const QsaState& draft, std::string& error, const SizeOf& size_of);
 
 /// Queue one layer's save / restore into a batch (validation happens here, before anything is queued).
 bool enqueue_kv_save(ConversationKv& image, const QsaState& st, const ModelGeometry& g, int64_t upto, bool index,

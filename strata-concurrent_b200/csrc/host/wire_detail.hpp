@@ -10,6 +10,7 @@
 
 #include <functional>
 #include <string>
+#include <unordered_map>
 #include <vector>
 
 namespace strata::core::wire_detail {
@@ -31,5 +32,19 @@ bool plan(const SavedConversation& image, int max_depth, const SizeOf& size_of, 
 /// up to the blob pool - into `out`.
 bool write_records(const SavedConversation& image, const WireIdentity& identity, const WirePlan& plan,
                    const std::vector<PlannedBlob>& blobs, const SizeOf& size_of, uint8_t* out, std::string& error);
+
+/// Where a blob lies in a payload.
+struct BlobAt {
+    uint64_t off = 0;
+    uint64_t bytes = 0;
+};
+using BlobTable = std::unordered_map<const void*, BlobAt>;
+
+/// Decode the record stream of `source` into a SHAPE image, in place: every metadata field real, every blob left
+/// empty and recorded in `blobs` under the address of its buffer or vector inside `image`.  Every check of a full
+/// decode runs except the payload hash; no blob byte is read, so `source` only has to serve the records (its size
+/// is the whole payload's).
+bool decode_shape(const WireSource& source, SavedConversation& image, WireDecoded& info, const WireExpect& expect,
+                  BlobTable& blobs, std::string& error);
 
 }  // namespace strata::core::wire_detail

@@ -300,7 +300,7 @@ int main(int argc, char** argv) {
     const double encode_ms = ms_since(t0);
 
     // ---- the device-side pack: the same payload straight from the permuted pool, no host image in between
-    double pack_ms = 0, pack_hash_ms = 0, pack_dev_ms = 0;
+    double pack_ms = 0, pack_hash_ms = 0, pack_dev_ms = 0, mount_dev_ms = 0;
     {
         WirePlan plan;
         check_ok(conversation_wire_pack_plan(view, a.ss, g, a.draft, plan, err), err, "device pack planned");
@@ -363,6 +363,73 @@ int main(int argc, char** argv) {
                                              plan.total_bytes - 1, used, denc, err),
               "a destination one byte short is refused");
         check(err.find("needs") != std::string::npos, "and the refusal names the size");
+
+        // ---- the device mount: that device-resident payload straight into a differently permuted pool
+        {
+            DeviceSession c(g, T, 4096, 37);
+            check(c.slots[0] != a.slots[0], "the mount target's placement differs from the source's");
+            WireExpect ex;
+            ex.check_geometry = true;
+            ex.geometry = img.geometry;
+            ex.check_hashes = true;
+            ex.geom_hash = geom_hash;
+            ex.pack_hash = pack_hash;
+            SavedConversation meta;
+            WireDecoded dinfo;
+            // refusals first: nothing may be written
+            const auto before = c.get(0, 0);
+            {
+                WireExpect wrong = ex;
+                wrong.pack_hash ^= 1;
+                check(conversation_wire_mount_device(on_device, plan.total_bytes, c.ss, g, c.draft, wrong, meta, dinfo,
+                                                     err) == ConversationRestore::invalid,
+                      "a payload for another pack is refused");
+                SessionState fewer = c.ss;
+                fewer.qsa_alloc -= 1;   // a session that owns one QSA layer less than the image carries
+                check(conversation_wire_mount_device(on_device, plan.total_bytes, fewer, g, c.draft, ex, meta, dinfo,
+                                                     err) == ConversationRestore::invalid,
+                      "an image for another layer carve is refused");
+                uint8_t* bad = nullptr;
+                cuda(cudaMalloc(&bad, plan.total_bytes), "corrupt copy");
+                cuda(cudaMemcpy(bad, on_device, plan.total_bytes, cudaMemcpyDeviceToDevice), "corrupt copy");
+                const uint8_t flip = 0x10;
+                cuda(cudaMemcpy(bad + 6, &flip, 1, cudaMemcpyHostToDevice), "flip a header flag bit");
+                check(conversation_wire_mount_device(bad, plan.total_bytes, c.ss, g, c.draft, ex, meta, dinfo, err) ==
+                          ConversationRestore::invalid,
+                      "a corrupted header is refused");
+                cudaFree(bad);
+                check(c.get(0, 0) == before, "and none of the refusals wrote anything");
+            }
+            t0 = std::chrono::steady_clock::now();
+            check(conversation_wire_mount_device(on_device, plan.total_bytes, c.ss, g, c.draft, ex, meta, dinfo, err) ==
+                      ConversationRestore::restored,
+                  ("device mount of the device payload: " + err).c_str());
+            mount_dev_ms = ms_since(t0);
+            check(meta.live.ids == content.ids && meta.live.gdn.empty() && meta.kv.size() == img.kv.size(),
+                  "the mount's metadata: the ids on the host, the bytes on the device");
+            for (size_t j = 0; j < img.kv.size(); ++j) {
+                check(c.get(j, 0) == content.k[j], "device-mounted K reads back through the destination table");
+                check(c.get(j, 1) == content.v[j], "device-mounted V reads back through the destination table");
+            }
+            check(from_device(c.gdn, content.gdn.size()) == content.gdn, "device-mounted GDN rows");
+            for (size_t j = 0; j < c.qsa.size(); ++j) {
+                const QsaState& st = c.qsa[j];
+                check(from_device(st.idx_tail, content.tail[j].size()) == content.tail[j], "device-mounted indexer tail");
+                check(from_device(st.idx_dead, content.dead[j].size()) == content.dead[j], "device-mounted dead key");
+                check(from_device(st.idx_block_pos, 1)[0] == content.block_pos[j], "device-mounted block position");
+                const size_t rows = (size_t) (T / 4), dim = (size_t) g.idx_key_dim;
+                const auto pooled = from_device(st.idx_pooled, (rows + 1) * dim);
+                check(std::equal(pooled.begin(), pooled.begin() + rows * dim, content.pooled[j].begin()),
+                      "device-mounted pooled rows");
+                check(std::equal(pooled.begin() + rows * dim, pooled.end(), content.dead[j].begin()),
+                      "the spare pooled row is the dead key again");
+            }
+            check(c.ss.ple_prev[0] == content.ids[T - 2] && c.ss.ple_prev[1] == content.ids[T - 1],
+                  "the PLE window after a device mount");
+            uint64_t fp = 0;
+            check_ok(conversation_kv_verify(img.kv.back(), c.draft, g, T, false, fp, err), err,
+                     "read-back verify of the device-mounted draft");
+        }
         cudaFree(on_device);
         cudaFreeHost(pinned);
     }
@@ -442,8 +509,8 @@ int main(int argc, char** argv) {
     std::printf("park %.2f ms, mount %.2f ms for %.1f MB of K/V + state (%llu payload bytes)\n", park_ms, mount_ms,
                 (double) img.bytes() / 1e6, (unsigned long long) enc.bytes);
     std::printf("host encode %.2f ms; device pack %.2f ms to pinned host (%.2f ms with the FNV pass), %.2f ms to "
-                "device memory\n",
-                encode_ms, pack_ms, pack_hash_ms, pack_dev_ms);
+                "device memory; device mount %.2f ms\n",
+                encode_ms, pack_ms, pack_hash_ms, pack_dev_ms, mount_dev_ms);
     std::printf("snapshot_gpu_test: %d checks passed\n", checks);
     return 0;
 }
