@@ -1,0 +1,35 @@
+"""Host-only C++ test programs (tests/cpp/*_cpu_test.cpp), built against libstrata_kv.so and run here.
+
+handoff_device_cpu_test: the 256-byte device descriptor a hand-off slot carries on one node - round trip, every
+refusal, and its trip through a real HandoffArena slot (claim, write, publish, read, release).
+"""
+import os
+import subprocess
+import tempfile
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+SRC = os.path.join(ROOT, "tests", "cpp")
+BIN = os.path.join(SRC, "bin")
+PKG = os.path.join(ROOT, "strata-concurrent_b200")
+CUDA = "/usr/local/cuda"
+
+
+def build(name: str) -> str:
+    os.makedirs(BIN, exist_ok=True)
+    src = os.path.join(SRC, name + ".cpp")
+    out = os.path.join(BIN, name)
+    deps = [src, os.path.join(PKG, "libstrata_kv.so")]
+    if not os.path.exists(out) or any(os.path.getmtime(d) > os.path.getmtime(out) for d in deps):
+        subprocess.run(["g++", "-std=c++20", "-O2", "-I", os.path.join(ROOT, "include"), "-I", f"{CUDA}/include",
+                        "-o", out, src, "-L", PKG, "-lstrata_kv", f"-Wl,-rpath,{PKG}", "-L", f"{CUDA}/lib64",
+                        "-lcudart", f"-Wl,-rpath,{CUDA}/lib64"], check=True)
+    return out
+
+
+def test_device_descriptor_round_trip_refusals_and_slot():
+    exe = build("handoff_device_cpu_test")
+    with tempfile.TemporaryDirectory() as d:
+        r = subprocess.run([exe, d], capture_output=True, text=True, timeout=300,
+                           env=dict(os.environ, CUDA_VISIBLE_DEVICES=""))
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
+    assert "checks passed" in r.stdout

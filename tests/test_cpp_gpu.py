@@ -31,7 +31,8 @@ def build(name: str) -> str:
     os.makedirs(BIN, exist_ok=True)
     src = os.path.join(SRC, name + ".cpp")
     out = os.path.join(BIN, name)
-    deps = [src, os.path.join(PKG, "libstrata_kv.so"), os.path.join(ORACLE, "liboracle.so")]
+    deps = [src, os.path.join(SRC, "session_fixture.hpp"), os.path.join(PKG, "libstrata_kv.so"),
+            os.path.join(ORACLE, "liboracle.so")]
     if not os.path.exists(out) or any(os.path.getmtime(d) > os.path.getmtime(out) for d in deps):
         subprocess.run(["g++", "-std=c++20", "-O2", "-I", os.path.join(ROOT, "include"), "-I", ORACLE,
                         "-I", f"{CUDA}/include", "-o", out, src, "-L", PKG, "-lstrata_kv", f"-Wl,-rpath,{PKG}",
@@ -66,3 +67,17 @@ def test_reference_gpu_snapshot_suite_passes_against_the_drop_in(torch_cuda):
     print(r.stdout)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
     assert "conversation_snapshot_test:" in r.stdout and "checks passed" in r.stdout
+
+
+def test_split_role_handoff_through_a_device_descriptor(torch_cuda):
+    """Two processes, two GPUs: the prefill instance publishes a device descriptor in a hand-off slot, the decode
+    instance mounts straight from the prefill GPU's HBM (see the program's header)."""
+    if torch_cuda.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    import tempfile
+    exe = build("handoff_device_gpu_test")
+    with tempfile.TemporaryDirectory() as d:
+        r = subprocess.run([exe, d], capture_output=True, text=True, timeout=600)
+    print(r.stdout)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
+    assert "both instances passed" in r.stdout
