@@ -81,3 +81,11 @@ def test_split_role_handoff_through_a_device_descriptor(torch_cuda):
     print(r.stdout)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
     assert "both instances passed" in r.stdout
+
+
+def test_device_mount_agrees_with_host_mount_for_every_format_and_mode(torch_cuda):
+    exe = build("device_mount_formats_gpu_test")
+    r = subprocess.run([exe], capture_output=True, text=True, timeout=600)
+    print(r.stdout)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
+    assert "checks passed" in r.stdout
