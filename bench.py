@@ -60,6 +60,8 @@ def parse():
                          "mixed = N/2 prefill + N/2 decode GPUs, 64 log-uniform sequences, host parks (config 5); "
                          "auto = pairs, plus config 4 at N = 4 and config 5 at N = 8 embedded in the same line")
     ap.add_argument("--chunk-mb", type=int, default=32, help="fan-out chain: pipeline chunk size")
+    ap.add_argument("--mixed-order", default="serial", choices=["per-source", "serial"],
+                    help="config 5: a decode GPU pulls on one stream per source prefill GPU, or one sequence at a time")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     return ap.parse_args()
@@ -982,6 +984,12 @@ def run_mixed(args, torch) -> dict | None:
         keep += [tables, peer_pool]
         pulls.append((i, (skv.Segment * len(segs))(*segs), len(segs)))
     side = torch.cuda.Stream()
+    per_source = args.mixed_order == "per-source"
+    source_stream = {p: torch.cuda.Stream() for p in sorted(set(owner[i] for i in mine_in))}
+    tuning = skv.get_copy_tuning()
+    if per_source:
+        # one issuing CTA per SM per pull (NVLink-bound, it needs no more) so up to three pulls share the GPU at once
+        skv.set_copy_tuning(tuning[0], tuning[1], 1, tuning[3])
     if decode:
         off = skv.image_offsets(kg, SLOT_TOKENS, kg.n_qsa)
         hosts = [skv.HostBuffer(off["total"]) for _ in range(SERVE_SLOTS)]
@@ -1005,14 +1013,22 @@ def run_mixed(args, torch) -> dict | None:
                 skv.resume(resume_segs[j], skv.PARK_STAGED, staging, staging.numel(), side)
         p1.record(side)
         for (i, arr, n), (a, b) in zip(pulls, ev):
-            a.record(stream)
-            skv.check(L.skv_copy(arr, n, skv.COPY_TMA, sp))
-            b.record(stream)
+            # one stream per source prefill GPU: pulls from different sources run at once, so a source that
+            # another decode GPU is also reading does not leave this GPU's NVLink ingress idle
+            st = source_stream[owner[i]] if per_source else stream
+            if st is not stream:
+                st.wait_event(h0)
+            a.record(st)
+            skv.check(L.skv_copy(arr, n, skv.COPY_TMA, st.cuda_stream))
+            b.record(st)
+        for st in set(source_stream.values()) if per_source else ():
+            stream.wait_stream(st)
         h1.record(stream)
         torch.cuda.synchronize()
         if it >= warmup:
             windows.append((h0.elapsed_time(h1), p0.elapsed_time(p1)))
             lat += [a.elapsed_time(b) for a, b in ev]
+    skv.set_copy_tuning(*tuning)
     status = torch.tensor([float(skv.query_status(local) != 0)], device="cuda")
     dist.all_reduce(status, op=dist.ReduceOp.MAX)
     win = torch.tensor([w[0] for w in windows], device="cuda")
@@ -1071,10 +1087,12 @@ def run_mixed(args, torch) -> dict | None:
                                    f"resume from pinned host memory",
                        "sequences": MIXED_SEQUENCES, "mean_tokens": round(float(np.mean(lengths)), 1),
                        "bytes_per_step": total, "serve_slots": SERVE_SLOTS, "slot_tokens": SLOT_TOKENS,
+                       "order": args.mixed_order,
                        "parallelism": f"{world // 2} prefill + {world // 2} decode"},
             "handoffs": {"per_decode_gpu_gbs": per_decode, "p50_ms": round(float(np.percentile(lat_all, 50)), 4),
                          "p99_ms": round(float(np.percentile(lat_all, 99)), 4),
-                         "max_ms": round(float(lat_all.max()), 4), "note": "per-sequence device time of its pull"},
+                         "max_ms": round(float(lat_all.max()), 4),
+                         "note": "per-sequence device time of its pull (concurrent pulls share the links)"},
             "parks": {"per_decode_gpu_gbs": parks, "bytes_per_step_per_gpu": slot_bytes,
                       "note": "park + resume of every serve slot, staged, on a side stream during the handoffs"},
             "parity": bool(okt.item() == 1.0) and status.item() == 0,
