@@ -54,7 +54,9 @@ def parse():
     ap.add_argument("--engine", default="tma", choices=["tma", "vec"])
     ap.add_argument("--seed", type=int, default=1)
     ap.add_argument("--pool-blocks", type=int, default=4096, help="slots per pool (the configs use 4,096)")
-    ap.add_argument("--p2p", default="pull", choices=["pull", "push"], help="N > 1: which GPU runs the copy")
+    ap.add_argument("--p2p", default="pull", choices=["pull", "push", "push-tma"],
+                    help="N > 1: the decode GPU pulls (TMA loads of peer memory), or the prefill GPU pushes (vector "
+                         "engine remote stores, or TMA bulk stores to peer memory)")
     ap.add_argument("--scenario", default="auto", choices=["auto", "pairs", "fanout", "mixed"],
                     help="N > 1: pairs = N/2 prefill->decode pairs; fanout = one prefill to N-1 decodes (config 4); "
                          "mixed = N/2 prefill + N/2 decode GPUs, 64 log-uniform sequences, host parks (config 5); "
@@ -560,6 +562,7 @@ def run_pairs(args, torch) -> dict | None:
     L = skv.lib()
     n_blocks = max(args.pool_blocks, kg.n_qsa * kg.blocks(t))
     pull = args.p2p == "pull"
+    push_engine = skv.COPY_TMA if args.p2p == "push-tma" else skv.COPY_VEC
     seq = None
     mine = None
     if active:
@@ -603,7 +606,7 @@ def run_pairs(args, torch) -> dict | None:
 
             def step():
                 counter[0] += 1
-                skv.check(L.skv_copy(arr, len(segs), skv.COPY_VEC, sp))              # remote 16-byte stores
+                skv.check(L.skv_copy(arr, len(segs), push_engine, sp))               # remote stores
                 skv.check(L.skv_signal(peer_flag, counter[0], sp))                   # ARRIVED
         else:
             def step():
@@ -660,7 +663,7 @@ def run_pairs(args, torch) -> dict | None:
                              "unit": "GB/s", "frac": round(res["per_pair_gbs"] / NVLINK_PEER_COPY_GBS, 4),
                              "frac_of_nominal_900": round(res["per_pair_gbs"] / 900.0, 4),
                              "peak_kind": "measured peer copy per direction (profiling recipe); 900 nominal",
-                             "traffic": None, "kernel": "copy_tma_kernel" if pull else "copy_vec_kernel"},
+                             "traffic": None, "kernel": "copy_vec_kernel" if args.p2p == "push" else "copy_tma_kernel"},
                 "clocks": clk.summary()}
     torch.cuda.synchronize()
     dist.barrier()
