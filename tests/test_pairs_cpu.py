@@ -31,6 +31,29 @@ def test_state_layout():
         assert lay["flag"] + 8 <= lay["bytes"] and lay["bytes"] % 1024 == 0
 
 
+def test_relay_pieces_pair_park_and_resume_byte_for_byte():
+    """The e2e relay cuts every park segment and its resume twin at the same places: piece k of the park writes
+    exactly the host bytes piece k of the resume reads, and together they cover the whole image."""
+    kg = skv.KvGeometry()
+    t = 32768 + 5
+
+    class FakePool:                              # segments read only a pool's base address and block count
+        base, n_blocks = 1 << 40, 4096
+
+    src = skv.PooledSequence(kg, FakePool(), t, kg.n_qsa, None, 2 << 40, 3 << 40, 4 << 40)
+    host = 5 << 40
+    park = skv.pack_segments(src, host)
+    resume = skv.unpack_segments(host, src)
+    pieces = bench.relay_pieces(park, resume)
+    assert len(pieces) > len(park)
+    covered = 0
+    for p, r in pieces:
+        assert p.bytes == r.bytes and p.bytes <= bench.RELAY_CHUNK_BYTES
+        assert p.dst == r.src                   # the park piece's host range is the resume piece's host range
+        covered += p.bytes
+    assert covered == sum(s.bytes for s in park)
+
+
 def test_mixed_plan_is_seeded_and_log_uniform():
     a, b = bench.mixed_plan(8, 1), bench.mixed_plan(8, 1)
     assert a == b and a != bench.mixed_plan(8, 2)
