@@ -14,6 +14,7 @@
 #include "strata_kv/conversation_wire_device.hpp"
 
 #include "kv_stream_detail.h"
+#include "skv_internal.h"
 #include "snapshot_detail.hpp"
 #include "strata_kv.h"
 #include "wire_detail.hpp"
@@ -303,8 +304,16 @@ bool conversation_wire_pack_device(const ConversationView& view, const SessionSt
     if (on_device) {
         const DeviceScope on(dst_device);
         if (!device_sync(error)) return false;   // the session's producers are done before the reads
-        if (!cuda_ok(cudaMemsetAsync(dst + p.blob_pool_off, 0, p.blob_pool_bytes, nullptr), error, "pool clear") ||
-            !cuda_ok(cudaMemcpyAsync(dst, records.data(), records.size(), cudaMemcpyHostToDevice, nullptr), error,
+        // only the pads between blobs (and after the last) need zeros: every other pool byte is gathered
+        std::vector<std::pair<uint64_t, uint64_t>> pads;
+        uint64_t cursor = p.blob_pool_off;
+        for (const Placed& pl : placed) {
+            if (pl.at > cursor) pads.emplace_back(cursor, pl.at - cursor);
+            cursor = std::max(cursor, pl.at + pl.piece->bytes);
+        }
+        if (p.total_bytes > cursor) pads.emplace_back(cursor, p.total_bytes - cursor);
+        if (skv::zero_ranges(dst, pads, nullptr) != SKV_OK) return pfail(error, skv_last_error());
+        if (!cuda_ok(cudaMemcpyAsync(dst, records.data(), records.size(), cudaMemcpyHostToDevice, nullptr), error,
                      "records"))
             return false;
         if (skv_clear_status(dst_device, nullptr) != SKV_OK) return pfail(error, skv_last_error());

@@ -575,6 +575,41 @@ int launch_copy_chained(const CopyPlan& plan, uint64_t total_tiles, const ChainA
     return e == cudaSuccess ? SKV_OK : cuda_fail(e, "chained copy kernel launch");
 }
 
+namespace {
+constexpr int kZeroBatch = 256;
+struct ZeroRanges {
+    uint8_t* base;
+    int n;
+    uint32_t len[kZeroBatch];
+    uint64_t off[kZeroBatch];
+};
+/// One CTA per range (grid-stride over ranges): byte stores of zero.  For the few short pads of a payload.
+__global__ void zero_ranges_kernel(const __grid_constant__ ZeroRanges z) {
+    for (int r = blockIdx.x; r < z.n; r += gridDim.x)
+        for (uint32_t i = threadIdx.x; i < z.len[r]; i += blockDim.x) z.base[z.off[r] + i] = 0;
+}
+}  // namespace
+
+int zero_ranges(uint8_t* base, const std::vector<std::pair<uint64_t, uint64_t>>& ranges, cudaStream_t stream) {
+    ZeroRanges z;
+    z.base = base;
+    for (size_t i = 0; i < ranges.size();) {
+        z.n = 0;
+        for (; i < ranges.size() && z.n < kZeroBatch; ++i) {
+            if (ranges[i].second == 0) continue;
+            if (ranges[i].second > UINT32_MAX) return fail(SKV_EINVAL, "zero_ranges: a range above 4 GiB");
+            z.off[z.n] = ranges[i].first;
+            z.len[z.n] = (uint32_t) ranges[i].second;
+            ++z.n;
+        }
+        if (!z.n) continue;
+        zero_ranges_kernel<<<std::min(z.n, 1024), 64, 0, stream>>>(z);
+        const cudaError_t e = cudaGetLastError();
+        if (e != cudaSuccess) return cuda_fail(e, "zero_ranges");
+    }
+    return SKV_OK;
+}
+
 int launch_signal(uint64_t* flag, uint64_t value, cudaStream_t stream) {
     signal_kernel<<<1, 1, 0, stream>>>(flag, value);
     const cudaError_t e = cudaGetLastError();

@@ -7,6 +7,8 @@
 
 #include <cstdint>
 #include <string>
+#include <utility>
+#include <vector>
 
 namespace skv {
 
@@ -98,6 +100,8 @@ int launch_copy(const CopyPlan& plan, uint64_t total_tiles, int engine, DeviceCt
 /// Launch the chained TMA kernel (the counters are reset on `stream` first).
 int launch_copy_chained(const CopyPlan& plan, uint64_t total_tiles, const ChainArgs& chain, DeviceCtx& ctx,
                         cudaStream_t stream);
+/// Zero the byte ranges (offset, length) of `base` (device memory) on `stream`: the alignment pads of a payload.
+int zero_ranges(uint8_t* base, const std::vector<std::pair<uint64_t, uint64_t>>& ranges, cudaStream_t stream);
 /// Enqueue the flag kernels.
 int launch_signal(uint64_t* flag, uint64_t value, cudaStream_t stream);
 int launch_wait(const uint64_t* flag, uint64_t value, uint64_t timeout_ns, uint32_t* status, cudaStream_t stream);

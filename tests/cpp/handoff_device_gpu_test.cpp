@@ -9,7 +9,7 @@
 // (handoff_device_mount), checks every byte against the oracle's content, and sends ACK <nonce>; the parent then
 // releases the slot.  Every wait is bounded (poll with a deadline).
 //
-// Usage: handoff_device_gpu_test <directory for the arena>      (exit 0 = pass, 77 = fewer than two GPUs)
+// Usage: handoff_device_gpu_test <directory for the arena> [tokens]   (exit 0 = pass, 77 = fewer than two GPUs)
 #include "session_fixture.hpp"
 #include "strata_kv/handoff_device.hpp"
 
@@ -26,7 +26,7 @@ namespace {
 
 constexpr uint64_t kGeomHash = 0x1111222233334444ull, kPackHash = 0x5555666677778888ull;
 constexpr uint64_t kClient = 7, kRequest = 1;
-constexpr int64_t T = 4096;
+int64_t T = 4096;   // tokens (argv[2]); config 1's length by default
 constexpr int kRounds = 5;   // the first hand-off pays the module loads, the IPC import and peer enablement
 
 ModelGeometry config_geometry() {
@@ -56,7 +56,7 @@ std::string recv_line(int fd, int ms) {
 int prefill(const std::string& dir, int to_decode, int from_decode, pid_t decode_pid) {
     cuda(cudaSetDevice(0), "cudaSetDevice(0)");
     const ModelGeometry g = config_geometry();
-    DeviceSession a(g, T, 4096, 11);
+    DeviceSession a(g, T, std::max<int64_t>(4096, 13 * ((T + 255) / 256) + 64), 11);
     const Content content = make_content(a, 1);
     upload(a, content);
     cuda(cudaDeviceSynchronize(), "upload");
@@ -109,7 +109,7 @@ int prefill(const std::string& dir, int to_decode, int from_decode, pid_t decode
 int decode(const std::string& dir, int from_prefill, int to_prefill) {
     cuda(cudaSetDevice(1), "cudaSetDevice(1)");
     const ModelGeometry g = config_geometry();
-    DeviceSession c(g, T, 4096, 37);
+    DeviceSession c(g, T, std::max<int64_t>(4096, 13 * ((T + 255) / 256) + 64), 37);
     const Content content = make_content(c, 1);   // the oracle's content: what the prefill instance holds
     std::string err;
     HandoffArena arena;
@@ -170,6 +170,8 @@ int decode(const std::string& dir, int from_prefill, int to_prefill) {
 
 int main(int argc, char** argv) {
     const std::string dir = argc > 1 ? argv[1] : "/tmp";
+    if (argc > 2) T = std::strtoll(argv[2], nullptr, 10);
+    if (T < 1 || T > 131072) return 2;
     int p2d[2], d2p[2];
     if (pipe(p2d) != 0 || pipe(d2p) != 0) return 2;
     const pid_t child = fork();   // before any CUDA call in either process

@@ -69,7 +69,8 @@ def test_reference_gpu_snapshot_suite_passes_against_the_drop_in(torch_cuda):
     assert "conversation_snapshot_test:" in r.stdout and "checks passed" in r.stdout
 
 
-def test_split_role_handoff_through_a_device_descriptor(torch_cuda):
+@pytest.mark.parametrize("tokens", [4096, 32768])
+def test_split_role_handoff_through_a_device_descriptor(torch_cuda, tokens):
     """Two processes, two GPUs: the prefill instance publishes a device descriptor in a hand-off slot, the decode
     instance mounts straight from the prefill GPU's HBM (see the program's header)."""
     if torch_cuda.cuda.device_count() < 2:
@@ -77,7 +78,7 @@ def test_split_role_handoff_through_a_device_descriptor(torch_cuda):
     import tempfile
     exe = build("handoff_device_gpu_test")
     with tempfile.TemporaryDirectory() as d:
-        r = subprocess.run([exe, d], capture_output=True, text=True, timeout=600)
+        r = subprocess.run([exe, d, str(tokens)], capture_output=True, text=True, timeout=600)
     print(r.stdout)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
     assert "both instances passed" in r.stdout
