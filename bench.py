@@ -165,6 +165,7 @@ class SeqOnGpu:
             self.pool_mem = None
             self.pool = skv.Pool(dev, n_blocks, kg.block_bytes)
             self.state = skv.Pool(dev, 1, lay["bytes"])
+            self.state_bytes = lay["bytes"]
             self.gdn, self.ids = self.state.base, self.state.base + lay["ids"]
             self.flag = self.state.base + lay["flag"]
             zero = torch.zeros(lay["bytes"], dtype=torch.uint8, device="cuda")
@@ -542,6 +543,111 @@ def summarize_pairs(max_elapsed_ms: float, per_step_ms: np.ndarray, pairs: int, 
             "p50_ms": float(np.percentile(per_step_ms, 50)), "p99_ms": float(np.percentile(per_step_ms, 99))}
 
 
+def pair_parity(torch, dist, seq, role: str, peer: int, active: bool):
+    """Each side packs its copy through ITS OWN table with the gather kernel; the decode side ships its image to
+    the prefill side, which compares it with the image of the source.  A 1-element tensor, 1.0 when every pair
+    agrees (MIN over ranks)."""
+    ok = torch.ones(1, device="cuda")
+    if active:
+        image = seq.packed(torch)
+        if role == "decode":
+            dist.send(image, peer)
+        else:
+            got = torch.empty_like(image)
+            dist.recv(got, peer)
+            ok[0] = float(bool(torch.equal(got, image)))
+    dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+    return ok
+
+
+def host_relay_pairs(args, torch, dist, kg, t: int, seq, role: str, peer: int, active: bool, stream,
+                     pairs: int) -> dict:
+    """e2e at N GPUs: the same hand-off through pinned host memory, the route the reference's multi-GPU split
+    takes.  The prefill rank parks into a shared-memory buffer both ranks registered with CUDA
+    (skv.SharedHostBuffer) and the decode rank resumes from it, piece by piece: after each piece's device-to-host
+    copy the prefill GPU raises that piece's flag in the same host buffer, the decode GPU waits for it (bounded) and
+    copies the piece in, so both PCIe links and both directions stay busy; the decode GPU raises DONE at the end.
+    C-ABI calls only (skv_park, skv_resume, skv_signal, skv_wait_flag).  The decode pool is cleared first and the
+    pairs' parity is checked again afterwards."""
+    L = skv.lib()
+    sp = stream.cuda_stream
+    off = skv.image_offsets(kg, t, kg.n_qsa)
+    shared, handle = None, None
+    if active and role == "prefill":
+        shared = skv.SharedHostBuffer(off["total"] + 8 * FLAGS)   # a fresh memfd reads as zeros: flags start at 0
+        handle = shared.handle()
+    handles = [None] * dist.get_world_size()
+    dist.all_gather_object(handles, handle)
+    if active and role == "decode":
+        shared = skv.SharedHostBuffer(off["total"] + 8 * FLAGS, handle=handles[peer])
+    steps, warmup = max(3, min(args.steps, 20)), 2
+    step = None
+    counter = [0]
+    if active:
+        flags = shared.ptr + off["total"]
+        done = flags + 8 * (FLAGS - 1)
+        staging = torch.empty(off["total"] + 256 * 64, dtype=torch.uint8, device="cuda")
+        if role == "prefill":
+            segs = [p for s in skv.pack_segments(seq.ps, shared.ptr) for p in skv.split_segment(s, RELAY_CHUNK_BYTES)]
+        else:
+            segs = [p for s in skv.unpack_segments(shared.ptr, seq.ps) for p in skv.split_segment(s, RELAY_CHUNK_BYTES)]
+        if len(segs) > FLAGS - 1:
+            raise SystemExit(f"{len(segs)} relay pieces; at most {FLAGS - 1}")
+        at, coff = 0, []
+        for p in segs:
+            coff.append(at)
+            at += (p.bytes + 255) & ~255
+        arrs = [(skv.Segment * 1)(p) for p in segs]
+        base = staging.data_ptr()
+        if role == "decode":   # the P2P run already filled this pool: clear it, the bytes must come from the host
+            zero = torch.zeros(256 << 20, dtype=torch.uint8, device="cuda")
+            for region, total in ((seq.pool.base, seq.pool.n_blocks * kg.block_bytes), (seq.state.base, seq.state_bytes)):
+                for a in range(0, total, zero.numel()):
+                    skv.copy([skv.segment(zero, region + a, min(zero.numel(), total - a))], skv.COPY_VEC)
+            torch.cuda.synchronize()
+
+        def step():
+            counter[0] += 1
+            v = counter[0]
+            if role == "prefill":
+                skv.check(L.skv_wait_flag(done, v - 1, 5_000_000_000, sp))        # the host buffer is free again
+                for k, a in enumerate(arrs):
+                    skv.check(L.skv_park(a, 1, skv.PARK_STAGED, base + coff[k], staging.numel() - coff[k], sp))
+                    skv.check(L.skv_signal(flags + 8 * k, v, sp))                  # piece k is in host memory
+            else:
+                for k, a in enumerate(arrs):
+                    skv.check(L.skv_wait_flag(flags + 8 * k, v, 5_000_000_000, sp))
+                    skv.check(L.skv_resume(a, 1, skv.PARK_STAGED, base + coff[k], staging.numel() - coff[k], sp))
+                skv.check(L.skv_signal(done, v, sp))                               # the host buffer may be reused
+    dist.barrier()
+    for _ in range(warmup):
+        if step:
+            step()
+    torch.cuda.synchronize()
+    dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        if step:
+            step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    dist.barrier()
+    el = torch.tensor([e0.elapsed_time(e1), float(skv.query_status(torch.cuda.current_device()) != 0)], device="cuda")
+    dist.all_reduce(el, op=dist.ReduceOp.MAX)
+    ok = pair_parity(torch, dist, seq, role, peer, active)
+    if shared is not None:
+        shared.close()
+    b = kg.metric_bytes(t)
+    value = pairs * b * steps / (float(el[0].item()) / 1e3) / 1e9
+    return {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": pairs * b, "d2h_bytes_per_step": pairs * b,
+            "ms_per_step": round(float(el[0].item()) / steps, 4), "per_pair_gbs": round(value / pairs, 3),
+            "parity": bool(ok.item() == 1.0) and el[1].item() == 0, "steps": steps,
+            "api": "skv_park on the prefill GPU into pinned memory shared with its decode rank (memfd + "
+                   "skv_host_register), skv_resume on the decode GPU, per-piece flags in that host memory",
+            "note": "the reference's multi-GPU route (through pinned RAM), PCIe-bound per pair"}
+
+
 def run_pairs(args, torch) -> dict | None:
     """N/2 prefill->decode pairs.  pull (default): the decode GPU's copy kernel reads the prefill GPU's pool
     pages over NVLink (TMA bulk loads from peer memory, no multicast) and writes its own pool; push: the
@@ -634,18 +740,8 @@ def run_pairs(args, torch) -> dict | None:
     red = torch.tensor([ev[0].elapsed_time(ev[args.steps]), float(status != 0)], device="cuda")
     dist.all_reduce(red, op=dist.ReduceOp.MAX)
     dist.all_reduce(per, op=dist.ReduceOp.MAX)
-    # parity: each side packs its copy through ITS OWN table with the gather kernel; the decode side ships
-    # its image to the prefill side, which compares it with the image of the source
-    ok = torch.ones(1, device="cuda")
-    if active:
-        image = seq.packed(torch)
-        if role == "decode":
-            dist.send(image, peer)
-        else:
-            got = torch.empty_like(image)
-            dist.recv(got, peer)
-            ok[0] = float(bool(torch.equal(got, image)))
-    dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+    ok = pair_parity(torch, dist, seq, role, peer, active)
+    e2e = None if args.no_e2e else host_relay_pairs(args, torch, dist, kg, t, seq, role, peer, active, stream, pairs)
     res = summarize_pairs(float(red[0].item()), per.cpu().numpy(), pairs, kg.metric_bytes(t), args.steps)
     line = None
     if rank == 0:
@@ -665,6 +761,8 @@ def run_pairs(args, torch) -> dict | None:
                              "peak_kind": "measured peer copy per direction (profiling recipe); 900 nominal",
                              "traffic": None, "kernel": "copy_vec_kernel" if args.p2p == "push" else "copy_tma_kernel"},
                 "clocks": clk.summary()}
+        if e2e is not None:
+            line["e2e"] = e2e
     torch.cuda.synchronize()
     dist.barrier()
     for p in imported:

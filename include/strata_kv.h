@@ -157,6 +157,10 @@ SKV_API int skv_clear_status(int device, void* stream);
  * run asynchronously on a side stream at PCIe speed. */
 SKV_API int skv_host_alloc(uint64_t bytes, void** out);
 SKV_API int skv_host_free(void* p);
+/* Page-lock and device-map memory the caller already owns (no reference counterpart): e.g. a shared-memory
+ * mapping two processes on one node both register, so one GPU parks into it and another resumes from it. */
+SKV_API int skv_host_register(void* p, uint64_t bytes);
+SKV_API int skv_host_unregister(void* p);
 
 /* Park: move the segments (paged device sources) into pinned host memory.  mode SKV_PARK_DIRECT writes
  * the host image from the kernel through the mapping; SKV_PARK_STAGED gathers into `staging` (device, at

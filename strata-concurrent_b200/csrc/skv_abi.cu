@@ -442,6 +442,27 @@ int skv_host_free(void* p) {
     return e == cudaSuccess ? SKV_OK : cuda_fail(e, "skv_host_free");
 }
 
+int skv_host_register(void* p, uint64_t bytes) {
+    if (!p || !bytes) return fail(SKV_EINVAL, "skv_host_register: bad arguments");
+    cudaError_t e = cudaHostRegister(p, (size_t) bytes, cudaHostRegisterPortable | cudaHostRegisterMapped);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaHostRegister");
+    // kernels (flags, direct copies) use the host address itself: the device must map it at the same address
+    void* dev = nullptr;
+    e = cudaHostGetDevicePointer(&dev, p, 0);
+    if (e != cudaSuccess || dev != p) {
+        (void) cudaGetLastError();
+        cudaHostUnregister(p);
+        return fail(SKV_EINVAL, "skv_host_register: this device does not map registered memory at its host address");
+    }
+    return SKV_OK;
+}
+
+int skv_host_unregister(void* p) {
+    if (!p) return SKV_OK;
+    const cudaError_t e = cudaHostUnregister(p);
+    return e == cudaSuccess ? SKV_OK : cuda_fail(e, "cudaHostUnregister");
+}
+
 /// STAGED transfers: the staging layout is the segments' bytes back to back, each 256-byte aligned.
 static int staged_offsets(const skv_segment* segs, int n, uint64_t staging_bytes, std::vector<uint64_t>& off) {
     off.assign((size_t) n, 0);

@@ -72,6 +72,8 @@ _SIGNATURES = {
     "skv_clear_status": ([C.c_int, C.c_void_p], C.c_int),
     "skv_host_alloc": ([C.c_uint64, C.POINTER(C.c_void_p)], C.c_int),
     "skv_host_free": ([C.c_void_p], C.c_int),
+    "skv_host_register": ([C.c_void_p, C.c_uint64], C.c_int),
+    "skv_host_unregister": ([C.c_void_p], C.c_int),
     "skv_park": ([C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_uint64, C.c_void_p], C.c_int),
     "skv_resume": ([C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_uint64, C.c_void_p], C.c_int),
     "skv_enable_peer": ([C.c_int, C.c_int], C.c_int),
@@ -204,6 +206,39 @@ def park(segs: list, mode: int, staging=None, staging_bytes: int = 0, stream=Non
 def resume(segs: list, mode: int, staging=None, staging_bytes: int = 0, stream=None) -> None:
     arr = (Segment * len(segs))(*segs)
     check(lib().skv_resume(arr, len(segs), mode, _ptr(staging), staging_bytes, _stream(stream)))
+
+
+class SharedHostBuffer:
+    """Pinned, device-mapped memory shared by the processes of one node: an anonymous shared-memory file (memfd)
+    that the creator sizes and every user maps and registers with CUDA (skv_host_register).  `handle()` gives what
+    another process needs to map the same pages: (pid, fd)."""
+
+    def __init__(self, nbytes: int, handle: tuple | None = None):
+        import mmap
+        import os
+        if handle is None:
+            self.fd = os.memfd_create("skv-shared-host", 0)
+            os.ftruncate(self.fd, nbytes)
+        else:
+            pid, fd = handle
+            self.fd = os.open(f"/proc/{pid}/fd/{fd}", os.O_RDWR)
+        self.nbytes = nbytes
+        self.map = mmap.mmap(self.fd, nbytes, mmap.MAP_SHARED, mmap.PROT_READ | mmap.PROT_WRITE)
+        self.ptr = C.addressof(C.c_char.from_buffer(self.map))
+        check(lib().skv_host_register(self.ptr, nbytes))
+
+    def handle(self) -> tuple:
+        import os
+        return (os.getpid(), self.fd)
+
+    def close(self) -> None:
+        import os
+        if self.map is not None:
+            check(lib().skv_host_unregister(self.ptr))
+            self.ptr = 0
+            self.map.close()
+            os.close(self.fd)
+            self.map = None
 
 
 def ipc_export(dev_ptr: int) -> bytes:
