@@ -775,21 +775,23 @@ def run_pairs(args, torch) -> dict | None:
 
 def run_fanout(args, torch, tokens: int | None = None, steps: int | None = None) -> dict | None:
     """Config 4: rank 0 (prefill) holds one sequence; ranks 1..N-1 (decode) each receive the whole cache into
-    their own pool at independent random slots.  Three ways, each timed over the same K steps:
+    their own pool at independent random slots.  Four ways, each timed over the same K steps:
 
       p2p    every receiver pulls the whole sequence from rank 0's pool at once (the source's NVLink egress
              carries the cache N-1 times);
       nccl   rank 0 packs the sequence into a contiguous image (gather kernel), ncclBroadcast sends it, each
              receiver scatters it into its pool (the reference-style collective path);
       chain  receiver k pulls chunk c of the cache from receiver k-1's pool as soon as k-1 signals it landed, so
-             every NVLink hop carries the cache once and the hops overlap chunk by chunk.
+             every NVLink hop carries the cache once and the hops overlap chunk by chunk;
+      chain_push  the same pipeline driven from the sending side: GPU k bulk-stores chunk c from its own pool
+             into GPU k+1's pool and raises k+1's flag for it (no read requests cross NVLink).
 
     value = receivers x B(T) x K / max-over-ranks timed region (fan-out counts every receiver's bytes)."""
     import torch.distributed as dist
     rank, world, local = ranks()
     kg = skv.KvGeometry()
     t = tokens or args.tokens
-    n_steps = steps or n_steps
+    n_steps = steps or args.steps
     receivers = world - 1
     lay = state_layout(kg, t)
     stream = torch.cuda.current_stream()
@@ -939,6 +941,35 @@ def run_fanout(args, torch, tokens: int | None = None, steps: int | None = None)
                 skv.check(L.skv_signal(done0, counter[0], sp))
     clear_receiver()
     results["chain"] = timed(step) + (parity(),)
+
+    # ---- chain_push: GPU k stores chunk c into GPU k+1's pool, then raises k+1's flag c
+    counter[0] = 2 * 10 ** 6
+    if rank < receivers:
+        dn, tab = peer_seq(rank + 1)
+        keep.append(tab)
+        whole = skv.kv_segments_pool_to_pool(seq.ps, dn) + skv.state_segments(seq.ps, dn.gdn, dn.ids)
+        pieces = [p for w in whole for p in skv.split_segment(w, chunk_bytes)]
+        if len(pieces) > FLAGS - 1 - receivers:
+            raise SystemExit(f"--chunk-mb {args.chunk_mb} gives {len(pieces)} chunks; at most {FLAGS - 1 - receivers}")
+        groups = [(g0, (skv.Segment * len(pieces[g0:g0 + skv.MAX_SEGMENTS]))(*pieces[g0:g0 + skv.MAX_SEGMENTS]))
+                  for g0 in range(0, len(pieces), skv.MAX_SEGMENTS)]
+        down = peer(rank + 1)[1]
+        done_at = flag(seq.state.base if rank == 0 else peer(0)[1], DONE + receivers)
+
+        def step():
+            counter[0] += 1
+            for g0, arr in groups:
+                wait = flag(seq.state.base, g0) if rank else None
+                skv.check(L.skv_copy_chained(arr, len(arr), wait, flag(down, g0), counter[0], wait_ns, sp))
+            if rank and rank == receivers - 1:        # the last store into the last receiver has landed
+                skv.check(L.skv_signal(done_at, counter[0], sp))
+            if rank == 0 and receivers > 1:
+                skv.check(L.skv_wait_flag(done_at, counter[0], wait_ns, sp))
+    else:
+        def step():                                   # the last receiver only receives
+            counter[0] += 1
+    clear_receiver()
+    results["chain_push"] = timed(step) + (parity(),)
     status = torch.tensor([float(skv.query_status(local) != 0)], device="cuda")
     dist.all_reduce(status, op=dist.ReduceOp.MAX)
 
@@ -958,7 +989,8 @@ def run_fanout(args, torch, tokens: int | None = None, steps: int | None = None)
                 "warmup": args.warmup, "ms_per_step": m["ms_per_step"], "p50_ms": m["p50_ms"], "p99_ms": m["p99_ms"],
                 "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u8", "data": "synthetic",
                 "config": {"workload": f"config 4: 1 prefill GPU fans one {t}-token cache out to {receivers} decode "
-                                       f"GPUs (independent random tables); best of p2p / nccl broadcast / chained pull",
+                                       f"GPUs (independent random tables); best of p2p / nccl broadcast / chained pull / "
+                                       f"chained push",
                            "tokens": t, "receivers": receivers, "method": best, "chunk_mb": args.chunk_mb,
                            "l2": "inputs larger than L2", "parallelism": f"1 -> {receivers} fan-out"},
                 "methods": methods, "parity": all(v["parity"] for v in methods.values()) and status.item() == 0,
