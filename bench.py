@@ -62,8 +62,9 @@ def parse():
                          "mixed = N/2 prefill + N/2 decode GPUs, 64 log-uniform sequences, host parks (config 5); "
                          "auto = pairs, plus config 4 at N = 4 and config 5 at N = 8 embedded in the same line")
     ap.add_argument("--chunk-mb", type=int, default=32, help="fan-out chain: pipeline chunk size")
-    ap.add_argument("--mixed-order", default="per-source", choices=["per-source", "serial"],
-                    help="config 5: a decode GPU pulls on one stream per source prefill GPU, or one sequence at a time")
+    ap.add_argument("--mixed-order", default="phased", choices=["phased", "per-source", "serial"],
+                    help="config 5: a decode GPU pulls on one stream per source prefill GPU, or one sequence at a "
+                         "time, or in port-exclusive phases (phased_schedule)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     return ap.parse_args()
@@ -1027,6 +1028,81 @@ def mixed_plan(world: int, seed: int) -> dict:
             "target": [int(x) for x in rng.choice(decode, MIXED_SEQUENCES)]}
 
 
+def phased_schedule(plan: dict, sizes: list, world: int) -> dict:
+    """An order for config 5's pulls that keeps every NVLink port busy with ONE transfer at a time.
+
+    D[s][d] = the bytes prefill GPU s hands to decode GPU d.  No schedule ends before the busiest port (a prefill
+    GPU's egress or a decode GPU's ingress, M bytes) has carried its load.  Pad D with idle time to a matrix whose
+    rows and columns all sum to M, and split it (Birkhoff-von Neumann) into phases: in phase k every prefill GPU
+    feeds exactly one decode GPU for w_k bytes.  Each flow (s, d) - its sequences back to back, in an order the
+    caller picks - is cut at the phase boundaries, real bytes first, so a phase's share of a flow may end early
+    (idle padding).
+    Run as: every decode GPU pulls its phases in order on one stream; before pulling from s it waits until the
+    previous decode GPU that pulled from s is done (that GPU signals it).  Waits only point at earlier phases, so
+    no cycle; each port carries one transfer at a time, and the whole ends no later than M at the port rate.
+
+    Returns {"bound_bytes": M, "phases": [(perm, w)], "runs": {decode rank: [run]}}, a run being
+    {"phase", "src" (rank), "lo", "hi" (byte range of the flow src -> this decode GPU), "wait" (this GPU's flag
+    index or None), "signal" ((rank, flag index) or None)}; a decode GPU's flag index is its run index."""
+    import itertools
+    src_ranks = [r for r in range(world) if r % 2 == 0]
+    dst_ranks = [r for r in range(world) if r % 2 == 1]
+    n = len(dst_ranks)
+    D = np.zeros((n, n), dtype=np.int64)
+    for i, (o, d) in enumerate(zip(plan["owner"], plan["target"])):
+        D[src_ranks.index(o), dst_ranks.index(d)] += int(sizes[i])
+    M = int(max(D.sum(1).max(), D.sum(0).max()))
+    P = D.copy()
+    rdef, cdef = M - P.sum(1), M - P.sum(0)
+    i = j = 0
+    while i < n and j < n:                       # north-west corner: pad rows and columns up to M
+        x = min(rdef[i], cdef[j])
+        P[i, j] += x
+        rdef[i] -= x
+        cdef[j] -= x
+        i += rdef[i] == 0
+        j += cdef[j] == 0
+    phases = []
+    perms = list(itertools.permutations(range(n)))
+    while P.any():                               # every row and column still sums to the same amount
+        w, perm = max((min(int(P[s, p[s]]) for s in range(n)), p) for p in perms)
+        if w <= 0:
+            raise RuntimeError("no positive permutation: the padded matrix is not balanced")
+        phases.append((perm, w))
+        for s in range(n):
+            P[s, perm[s]] -= w
+    left = D.copy()                              # real bytes still to place, per flow
+    cursor = np.zeros((n, n), dtype=np.int64)    # bytes of each flow already placed
+    runs = {d: [] for d in dst_ranks}
+    last = {}                                    # source rank -> (decode rank, run index) of its latest real run
+    for k, (perm, w) in enumerate(phases):
+        for s in range(n):
+            d = perm[s]
+            real = int(min(w, left[s, d]))
+            if real == 0:
+                continue
+            left[s, d] -= real
+            dr, sr = dst_ranks[d], src_ranks[s]
+            run = {"phase": k, "src": sr, "lo": int(cursor[s, d]), "hi": int(cursor[s, d]) + real,
+                   "wait": None, "signal": None}
+            cursor[s, d] += real
+            idx = len(runs[dr])
+            prev = last.get(sr)
+            if prev is not None and prev[0] != dr:
+                run["wait"] = idx
+                runs[prev[0]][prev[1]]["signal"] = (dr, idx)
+            runs[dr].append(run)
+            last[sr] = (dr, idx)
+    return {"bound_bytes": M, "phases": phases, "runs": runs}
+
+
+def port_bound(plan: dict, sizes: list, world: int) -> dict:
+    """Config 5's schedule-independent bound: the busiest NVLink port's bytes at the measured peer-copy rate."""
+    m = phased_schedule(plan, sizes, world)["bound_bytes"]
+    ms = m / NVLINK_PEER_COPY_GBS / 1e6
+    return {"busiest_port_bytes": m, "ms": round(ms, 3), "gbs": round(sum(sizes) / ms / 1e6, 1)}
+
+
 class SeqSet:
     """Several sequences in ONE library-allocated block pool (CUDA-IPC exportable) plus one state arena with each
     sequence's GDN rows and ids (`state_layout` per sequence), every layer's blocks at seed-random slots."""
@@ -1072,11 +1148,17 @@ class SeqSet:
 def run_mixed(args, torch) -> dict | None:
     """Config 5: the even ranks prefill, the odd ranks decode.  64 sequences with seeded log-uniform lengths on
     [1K, 128K] live in their prefill owner's pool; each decode GPU pulls the sequences assigned to it (random
-    pairing, so several decode GPUs may read one prefill GPU at once) back to back, one skv_copy (TMA, peer
-    loads, no multicast) per sequence straight into its own pool.  Meanwhile a side stream on every decode GPU
-    parks its 8 serve slots (4,096-token conversations) to pinned host memory and resumes them (skv_park /
-    skv_resume, staged).  value = all 64 sequences' B(T) per step / the max-over-ranks handoff window; the
-    per-sequence latency is each pull's device time."""
+    pairing, so several decode GPUs may want one prefill GPU at once) with skv_copy (TMA, peer loads, no
+    multicast) straight into its own pool, in one of three orders (--mixed-order):
+
+      phased      (default) port-exclusive phases from phased_schedule: one stream, each prefill GPU read by one
+                  decode GPU at a time, hand-overs by device flags (skv_signal / skv_wait_flag);
+      per-source  one stream per source prefill GPU, one skv_copy per sequence, all sources at once;
+      serial      one skv_copy per sequence, back to back.
+
+    Meanwhile a side stream on every decode GPU parks its 8 serve slots (4,096-token conversations) to pinned
+    host memory and resumes them (skv_park / skv_resume, staged).  value = all 64 sequences' B(T) per step / the
+    max-over-ranks handoff window; a sequence's latency runs from the step's start to its last byte landing."""
     import torch.distributed as dist
     rank, world, local = ranks()
     kg = skv.KvGeometry()
@@ -1093,12 +1175,19 @@ def run_mixed(args, torch) -> dict | None:
     held = SeqSet(torch, kg, [lengths[i] for i in (mine_in if decode else mine_out)], args.seed + 7 * rank,
                   fill=not decode)
     slots = SeqSet(torch, kg, [SLOT_TOKENS] * (2 * SERVE_SLOTS), args.seed + 7 * rank + 3, fill=True) if decode else None
-    info = None if decode else {"pool": skv.ipc_export(held.pool.base), "state": skv.ipc_export(held.state.base),
-                                "n_blocks": held.n_blocks, "seqs": mine_out, "offs": held.offs, "blocks": held.blocks}
+    phased = args.mixed_order == "phased"
+    flags = None
+    if decode and phased:            # one 8-byte word per run of this GPU's phased order (phased_schedule)
+        flags = skv.Pool(local, 1, 4096)
+        zero = torch.zeros(512, dtype=torch.int64, device="cuda")
+        skv.copy([skv.segment(zero, flags.base, 4096)], skv.COPY_VEC)
+    info = {"flags": skv.ipc_export(flags.base) if flags else None} if decode else {
+        "pool": skv.ipc_export(held.pool.base), "state": skv.ipc_export(held.state.base),
+        "n_blocks": held.n_blocks, "seqs": mine_out, "offs": held.offs, "blocks": held.blocks}
     torch.cuda.synchronize()
     infos = [None] * world
     dist.all_gather_object(infos, info)
-    maps, keep, pulls = {}, [], []
+    maps, keep, pulls, segs_of = {}, [], [], {}
     for k, i in enumerate(mine_in if decode else []):
         p = owner[i]
         if p not in maps:
@@ -1116,6 +1205,26 @@ def run_mixed(args, torch) -> dict | None:
         segs = skv.kv_segments_pool_to_pool(src, dst) + skv.state_segments(src, dst.gdn, dst.ids)
         keep += [tables, peer_pool]
         pulls.append((i, (skv.Segment * len(segs))(*segs), len(segs)))
+        segs_of[i] = segs
+    runs, peer_flags = [], {}
+    if decode and phased:
+        stream_bytes = lambda t: (2 * kg.n_qsa * kg.pages(t) * kg.page_bytes + kg.gdn_bytes  # noqa: E731
+                                  + 16 * ((4 * t + 15) // 16))
+        assert all(sum(g.bytes for g in segs_of[i]) == stream_bytes(lengths[i]) for i in mine_in)
+        sched = phased_schedule(plan, [stream_bytes(t) for t in lengths], world)
+        for run in sched["runs"][rank]:
+            # a flow's sequences shortest first: the cuts are by bytes, so the order moves no phase, and most
+            # sequences land early
+            flow = sorted((i for i in mine_in if owner[i] == run["src"]), key=lambda i: (lengths[i], i))
+            ends = np.cumsum([stream_bytes(lengths[i]) for i in flow])
+            pieces = skv.slice_segments([g for i in flow for g in segs_of[i]], run["lo"], run["hi"])
+            arrays = [((skv.Segment * len(pieces[a:a + skv.MAX_SEGMENTS]))(*pieces[a:a + skv.MAX_SEGMENTS]),
+                       len(pieces[a:a + skv.MAX_SEGMENTS])) for a in range(0, len(pieces), skv.MAX_SEGMENTS)]
+            if run["signal"] and run["signal"][0] not in peer_flags:
+                peer_flags[run["signal"][0]] = skv.ipc_import(local, infos[run["signal"][0]]["flags"])
+            runs.append(dict(run, arrays=arrays,
+                             starts=[i for i, e in zip(flow, ends) if run["lo"] <= e - stream_bytes(lengths[i]) < run["hi"]],
+                             ends=[i for i, e in zip(flow, ends) if run["lo"] < e <= run["hi"]]))
     side = torch.cuda.Stream()
     per_source = args.mixed_order == "per-source"
     source_stream = {p: torch.cuda.Stream() for p in sorted(set(owner[i] for i in mine_in))}
@@ -1146,7 +1255,24 @@ def run_mixed(args, torch) -> dict | None:
                 skv.park(park_segs[j], skv.PARK_STAGED, staging, staging.numel(), side)
                 skv.resume(resume_segs[j], skv.PARK_STAGED, staging, staging.numel(), side)
         p1.record(side)
-        for (i, arr, n), (a, b) in zip(pulls, ev):
+        if phased:
+            # this GPU's runs in phase order on one stream; a run from a prefill GPU another decode GPU read
+            # before waits for that GPU's signal, and each run signals the next reader of its source
+            rev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in runs]
+            for j, (run, (a, b)) in enumerate(zip(runs, rev)):
+                if run["wait"] is not None:
+                    skv.check(L.skv_wait_flag(flags.base + 8 * run["wait"], it + 1, 5_000_000_000, sp))
+                a.record(stream)
+                for arr, n in run["arrays"]:
+                    skv.check(L.skv_copy(arr, n, skv.COPY_TMA, sp))
+                b.record(stream)
+                if run["signal"] is not None:
+                    r, idx = run["signal"]
+                    skv.check(L.skv_signal(peer_flags[r] + 8 * idx, it + 1, sp))
+            first = {i: rev[j][0] for j in reversed(range(len(runs))) for i in runs[j]["starts"]}
+            last = {i: rev[j][1] for j in range(len(runs)) for i in runs[j]["ends"]}
+            ev = [(first[i], last[i]) for i, _, _ in pulls]
+        for (i, arr, n), (a, b) in zip(pulls, ev) if not phased else ():
             # one stream per source prefill GPU: pulls from different sources run at once, so a source that
             # another decode GPU is also reading does not leave this GPU's NVLink ingress idle
             st = source_stream[owner[i]] if per_source else stream
@@ -1190,19 +1316,24 @@ def run_mixed(args, torch) -> dict | None:
     dist.all_reduce(okt, op=dist.ReduceOp.MIN)
     # gather per-rank facts to rank 0
     facts = {"lat": lat, "landed": landed, "park_ms": [w[1] for w in windows], "hand_ms": [w[0] for w in windows],
-             "bytes_in": sum(kg.metric_bytes(lengths[i]) for i in mine_in), "decode": decode}
+             "bytes_in": sum(kg.metric_bytes(lengths[i]) for i in mine_in), "decode": decode,
+             "launches": (sum(len(r["arrays"]) + (r["wait"] is not None) + (r["signal"] is not None) for r in runs)
+                          if phased else len(pulls))}
     allf = [None] * world
     dist.all_gather_object(allf, facts)
     torch.cuda.synchronize()
     dist.barrier()
-    del pulls, keep
+    del pulls, keep, runs
     for pool_base, state_base in maps.values():
         skv.ipc_close(pool_base)
         skv.ipc_close(state_base)
+    for ptr in peer_flags.values():
+        skv.ipc_close(ptr)
     dist.barrier()
     if rank != 0:
         return None
     total = sum(kg.metric_bytes(t) for t in lengths)
+    bound = port_bound(plan, [kg.metric_bytes(t) for t in lengths], world)
     wins = win.cpu().numpy()
     value = total * steps / (float(wins.sum()) / 1e3) / 1e9
     lat_all = np.concatenate([np.asarray(f["lat"]) for f in allf if f["lat"]])
@@ -1236,11 +1367,14 @@ def run_mixed(args, torch) -> dict | None:
             "parks": {"per_decode_gpu_gbs": parks, "bytes_per_step_per_gpu": slot_bytes,
                       "note": "park + resume of every serve slot, staged, on a side stream during the handoffs"},
             "parity": bool(okt.item() == 1.0) and status.item() == 0,
-            "gpu_launches": steps * (MIXED_SEQUENCES + len(dec) * SERVE_SLOTS * 2),
+            "gpu_launches": steps * (sum(f["launches"] for f in dec) + len(dec) * SERVE_SLOTS * 2),
             "roofline": {"bound": "nvlink", "achieved": round(mean_ingress, 1), "peak": NVLINK_PEER_COPY_GBS,
                          "unit": "GB/s", "frac": round(mean_ingress / NVLINK_PEER_COPY_GBS, 4),
                          "peak_kind": "measured peer copy per direction; mean decode-GPU ingress over its window",
-                         "traffic": None, "kernel": "copy_tma_kernel"}}
+                         "traffic": None, "kernel": "copy_tma_kernel"},
+            "port_bound": dict(bound, frac=round(value / bound["gbs"], 4),
+                               note="the busiest NVLink port's bytes (a prefill GPU's egress or a decode GPU's "
+                                    "ingress) at the measured peer-copy rate: no order of the pulls ends sooner")}
 
 
 def pack_image(torch, ps: skv.PooledSequence):
@@ -1262,7 +1396,7 @@ def brief(line: dict | None, keys=("value", "ms_per_step", "p50_ms", "p99_ms", "
     if line is None:
         return None
     out = {k: line[k] for k in keys if k in line}
-    for k in ("config", "methods", "roofline", "handoffs", "parks"):
+    for k in ("config", "methods", "roofline", "handoffs", "parks", "port_bound"):
         if k in line:
             out[k] = line[k]
     return out

@@ -139,25 +139,52 @@ def segment(src, dst, nbytes: int, *, src_pages=None, dst_pages=None, page_bytes
                    int(src_page_limit), int(dst_page_limit))
 
 
+def _segment_unit(seg: Segment) -> int:
+    """The granule a segment is cut on: a whole page when either side is paged, else 16 bytes."""
+    unit = seg.page_bytes if (seg.src_pages or seg.dst_pages) else 16
+    if unit <= 0 or seg.bytes % unit:
+        raise ValueError("a segment splits on whole pages (paged) or 16-byte units (contiguous)")
+    return unit
+
+
+def slice_segment(seg: Segment, start: int, end: int) -> Segment:
+    """Bytes [start, end) of one segment as a segment of its own; both ends must lie on the segment's granule
+    (a whole page when a side is paged, 16 bytes otherwise)."""
+    unit = _segment_unit(seg)
+    if start % unit or end % unit or not 0 <= start < end <= seg.bytes:
+        raise ValueError(f"slice [{start}, {end}) of a {seg.bytes}-byte segment is not on {unit}-byte granules")
+    first_page = start // unit if (seg.src_pages or seg.dst_pages) else 0
+    return Segment(
+        seg.src if seg.src_pages else (seg.src or 0) + start,
+        seg.dst if seg.dst_pages else (seg.dst or 0) + start,
+        seg.src_pages + 4 * first_page if seg.src_pages else None,
+        seg.dst_pages + 4 * first_page if seg.dst_pages else None,
+        end - start, seg.page_bytes, 0, seg.src_page_limit, seg.dst_page_limit)
+
+
 def split_segment(seg: Segment, max_bytes: int) -> list:
     """Cut one segment into pieces of at most `max_bytes` (whole pages for a paged side, 16-byte multiples for a
     contiguous one), in order: the pieces move exactly the bytes of the whole.  Used to pipeline a long copy
     chunk by chunk (a relay or a chained fan-out signals each piece as it lands)."""
-    paged = bool(seg.src_pages or seg.dst_pages)
-    unit = seg.page_bytes if paged else 16
-    if unit <= 0 or seg.bytes % unit:
-        raise ValueError("a segment splits on whole pages (paged) or 16-byte units (contiguous)")
+    unit = _segment_unit(seg)
     per = max(1, max_bytes // unit) * unit
-    out = []
-    for at in range(0, seg.bytes, per):
-        n = min(per, seg.bytes - at)
-        first_page = at // unit if paged else 0
-        out.append(Segment(
-            seg.src if seg.src_pages else seg.src + at,
-            seg.dst if seg.dst_pages else seg.dst + at,
-            seg.src_pages + 4 * first_page if seg.src_pages else None,
-            seg.dst_pages + 4 * first_page if seg.dst_pages else None,
-            n, seg.page_bytes, 0, seg.src_page_limit, seg.dst_page_limit))
+    return [slice_segment(seg, at, min(at + per, seg.bytes)) for at in range(0, seg.bytes, per)]
+
+
+def slice_segments(segs: list, start: int, end: int) -> list:
+    """Bytes [start, end) of a list of segments taken as one stream, in order.  A cut that falls inside a segment
+    is rounded down to that segment's granule, so adjacent slices [a, b) and [b, c) always tile the stream
+    exactly."""
+    out, at = [], 0
+    for seg in segs:
+        lo, hi = max(start, at), min(end, at + seg.bytes)
+        if lo < hi:
+            unit = _segment_unit(seg)
+            a = (lo - at) // unit * unit
+            b = seg.bytes if hi == at + seg.bytes else (hi - at) // unit * unit
+            if a < b:
+                out.append(slice_segment(seg, a, b))
+        at += seg.bytes
     return out
 
 

@@ -66,6 +66,71 @@ def test_mixed_plan_is_seeded_and_log_uniform():
     assert 20000 < np.mean(means) < 34000
 
 
+def _play(sched, rate):
+    """Run a phased schedule in an ideal model: a run starts when its GPU's previous run ended and, if it waits,
+    when the run that signals it ended; it moves its bytes at `rate`.  Returns the makespan; fails on a deadlock."""
+    runs = sched["runs"]
+    signaller = {r["signal"]: (d, j) for d, rs in runs.items() for j, r in enumerate(rs) if r["signal"]}
+    end, clock, at = {}, {d: 0.0 for d in runs}, {d: 0 for d in runs}
+    moved = True
+    while moved:
+        moved = False
+        for d, rs in runs.items():
+            while at[d] < len(rs):
+                j, r = at[d], rs[at[d]]
+                start = clock[d]
+                if r["wait"] is not None:
+                    assert r["wait"] == j
+                    dep = signaller[(d, j)]
+                    if dep not in end:
+                        break
+                    start = max(start, end[dep])
+                end[(d, j)] = clock[d] = start + (r["hi"] - r["lo"]) / rate
+                at[d] += 1
+                moved = True
+    assert all(at[d] == len(rs) for d, rs in runs.items()), "deadlock"
+    return max(clock.values())
+
+
+@pytest.mark.parametrize("world,seed", [(8, 1), (8, 2), (8, 7), (4, 1), (4, 3), (2, 1)])
+def test_phased_schedule_tiles_every_flow_and_meets_the_port_bound(world, seed):
+    plan = bench.mixed_plan(world, seed)
+    sizes = [24576 * t + 79036416 for t in plan["lengths"]]
+    sched = bench.phased_schedule(plan, sizes, world)
+    # the bound is the busiest port
+    egress = {s: sum(b for b, o in zip(sizes, plan["owner"]) if o == s) for s in range(0, world, 2)}
+    ingress = {d: sum(b for b, t in zip(sizes, plan["target"]) if t == d) for d in range(1, world, 2)}
+    assert sched["bound_bytes"] == max(max(egress.values()), max(ingress.values()))
+    # phases are permutations whose weights sum to the bound
+    assert sum(w for _, w in sched["phases"]) == sched["bound_bytes"]
+    assert all(sorted(p) == list(range(world // 2)) for p, _ in sched["phases"])
+    # every flow (src -> dst) is cut into consecutive byte ranges covering exactly its sequences
+    for d, rs in sched["runs"].items():
+        assert [r["phase"] for r in rs] == sorted(r["phase"] for r in rs)
+        for s in range(0, world, 2):
+            mine = [r for r in rs if r["src"] == s]
+            want = sum(b for b, o, t in zip(sizes, plan["owner"], plan["target"]) if o == s and t == d)
+            pos = 0
+            for r in mine:
+                assert r["lo"] == pos < r["hi"]
+                pos = r["hi"]
+            assert pos == want
+    # in each phase a source feeds at most one decode GPU; reads of one source are chained by signals
+    for k in range(len(sched["phases"])):
+        srcs = [r["src"] for rs in sched["runs"].values() for r in rs if r["phase"] == k]
+        assert len(srcs) == len(set(srcs))
+    # with every port at one rate, the order ends exactly at the port bound (and never deadlocks)
+    rate = 1e9
+    assert _play(sched, rate) == pytest.approx(sched["bound_bytes"] / rate, rel=1e-9)
+
+
+def test_port_bound_reports_the_busiest_port():
+    plan = {"lengths": [1, 1, 1], "owner": [0, 0, 2], "target": [1, 3, 3]}
+    b = bench.port_bound(plan, [100, 200, 300], 4)
+    assert b["busiest_port_bytes"] == 500          # decode GPU 3's ingress
+    assert b["ms"] == pytest.approx(500 / bench.NVLINK_PEER_COPY_GBS / 1e6, abs=1e-3)
+
+
 def test_summarize_pairs():
     per = np.linspace(1.0, 2.0, 100)
     r = bench.summarize_pairs(150.0, per, pairs=4, seq_bytes=10 ** 9, steps=100)

@@ -31,3 +31,43 @@ def test_contiguous_segment_splits_on_16_bytes():
 def test_a_ragged_segment_is_refused():
     with pytest.raises(ValueError):
         skv.split_segment(skv.segment(0, 0, 4096 + 16, src_pages=8, page_bytes=4096, src_page_limit=4), 4096)
+
+
+def _granules(seg):
+    """Each granule a segment moves, named by where it comes from and where it goes (table entry or address)."""
+    unit = seg.page_bytes if (seg.src_pages or seg.dst_pages) else 16
+    out = []
+    for g in range(seg.bytes // unit):
+        src = ("page", seg.src, (seg.src_pages or 0) + 4 * g) if seg.src_pages else ("addr", (seg.src or 0) + g * unit)
+        dst = ("page", seg.dst, (seg.dst_pages or 0) + 4 * g) if seg.dst_pages else ("addr", (seg.dst or 0) + g * unit)
+        out.append((src, dst, unit))
+    return out
+
+
+def test_slices_of_a_segment_stream_tile_it_exactly():
+    """Cut points anywhere (mid-page, mid-segment, on boundaries, repeated): the slices move every granule of the
+    stream exactly once, in order, whatever the rounding inside a segment."""
+    import numpy as np
+    segs = [skv.segment(0x10000, 0x20000, 4096 * 7, src_pages=0x100, dst_pages=0x200, page_bytes=4096,
+                        src_page_limit=50, dst_page_limit=60),
+            skv.segment(0x30000, 0x40000, 160),
+            skv.segment(0x50000, 0x60000, 4096 * 3, src_pages=0x300, page_bytes=4096, src_page_limit=9),
+            skv.segment(0x70000, 0x80000, 16)]
+    whole = [g for s in segs for g in _granules(s)]
+    total = sum(s.bytes for s in segs)
+    rng = np.random.default_rng(5)
+    for trial in range(200):
+        cuts = sorted(set([0, total] + [int(x) for x in rng.integers(0, total + 1, rng.integers(0, 8))]))
+        got = []
+        for a, b in zip(cuts, cuts[1:]):
+            for s in skv.slice_segments(segs, a, b):
+                got += _granules(s)
+        assert got == whole, cuts
+
+
+def test_slice_segment_refuses_cuts_off_the_granule():
+    s = skv.segment(0, 0, 4096 * 4, src_pages=8, page_bytes=4096, src_page_limit=4)
+    assert skv.slice_segment(s, 4096, 8192).bytes == 4096
+    for a, b in ((1, 4096), (0, 4095), (4096, 4096), (0, 4096 * 5)):
+        with pytest.raises(ValueError):
+            skv.slice_segment(s, a, b)
