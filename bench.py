@@ -1241,6 +1241,7 @@ def run_mixed(args, torch) -> dict | None:
     lat = []       # per-sequence pull times (ms), timed steps
     landed = []    # per-sequence time from the step's start (every sequence ready) to its last byte landing
     windows = []   # (handoff window, park window) per timed step, this rank
+    idle = []      # phased: per timed step, the window minus this GPU's copy time
     for it in range(warmup + steps):
         dist.barrier()
         torch.cuda.synchronize()
@@ -1289,6 +1290,8 @@ def run_mixed(args, torch) -> dict | None:
             windows.append((h0.elapsed_time(h1), p0.elapsed_time(p1)))
             lat += [a.elapsed_time(b) for a, b in ev]
             landed += [h0.elapsed_time(b) for a, b in ev]
+            if phased and runs:      # the share of the window this GPU spent waiting for hand-overs
+                idle.append(h0.elapsed_time(h1) - sum(a.elapsed_time(b) for a, b in rev))
     skv.set_copy_tuning(*tuning)
     status = torch.tensor([float(skv.query_status(local) != 0)], device="cuda")
     dist.all_reduce(status, op=dist.ReduceOp.MAX)
@@ -1317,6 +1320,7 @@ def run_mixed(args, torch) -> dict | None:
     # gather per-rank facts to rank 0
     facts = {"lat": lat, "landed": landed, "park_ms": [w[1] for w in windows], "hand_ms": [w[0] for w in windows],
              "bytes_in": sum(kg.metric_bytes(lengths[i]) for i in mine_in), "decode": decode,
+             "idle_ms": round(float(np.mean(idle)), 3) if idle else None,
              "launches": (sum(len(r["arrays"]) + (r["wait"] is not None) + (r["signal"] is not None) for r in runs)
                           if phased else len(pulls))}
     allf = [None] * world
@@ -1356,14 +1360,16 @@ def run_mixed(args, torch) -> dict | None:
                        "bytes_per_step": total, "serve_slots": SERVE_SLOTS, "slot_tokens": SLOT_TOKENS,
                        "order": args.mixed_order,
                        "parallelism": f"{world // 2} prefill + {world // 2} decode"},
-            "handoffs": {"per_decode_gpu_gbs": per_decode,
+            "handoffs": {"per_decode_gpu_gbs": per_decode, "idle_ms_per_decode_gpu": [f["idle_ms"] for f in dec],
                          "landed_p50_ms": round(float(np.percentile(landed_all, 50)), 4),
                          "landed_p99_ms": round(float(np.percentile(landed_all, 99)), 4),
                          "pull_p50_ms": round(float(np.percentile(lat_all, 50)), 4),
                          "pull_p99_ms": round(float(np.percentile(lat_all, 99)), 4),
                          "note": "landed: from the step's start (every sequence ready on its prefill GPU) to the "
                                  "sequence's last byte in the decode pool - the line's p50/p99; pull: the device time "
-                                 "of its own copy (concurrent pulls share the links)"},
+                                 "from its first byte's copy to its last byte's (concurrent pulls share the links; "
+                                 "phased: a sequence may span phases); idle: phased only, the window minus the GPU's "
+                                 "copy time (waits for hand-overs, idle padding)"},
             "parks": {"per_decode_gpu_gbs": parks, "bytes_per_step_per_gpu": slot_bytes,
                       "note": "park + resume of every serve slot, staged, on a side stream during the handoffs"},
             "parity": bool(okt.item() == 1.0) and status.item() == 0,
