@@ -1251,11 +1251,6 @@ def run_mixed(args, torch) -> dict | None:
         h0.record(stream)
         side.wait_stream(stream)
         p0.record(side)
-        if decode:
-            for j in range(SERVE_SLOTS):
-                skv.park(park_segs[j], skv.PARK_STAGED, staging, staging.numel(), side)
-                skv.resume(resume_segs[j], skv.PARK_STAGED, staging, staging.numel(), side)
-        p1.record(side)
         if phased:
             # this GPU's runs in phase order on one stream; a run from a prefill GPU another decode GPU read
             # before waits for that GPU's signal, and each run signals the next reader of its source
@@ -1282,6 +1277,13 @@ def run_mixed(args, torch) -> dict | None:
             a.record(st)
             skv.check(L.skv_copy(arr, n, skv.COPY_TMA, st.cuda_stream))
             b.record(st)
+        # the serve-slot parks are enqueued AFTER the pulls: their ~430 launches and copies take the host about a
+        # millisecond, which the pulls would otherwise wait out at the start of every step
+        if decode:
+            for j in range(SERVE_SLOTS):
+                skv.park(park_segs[j], skv.PARK_STAGED, staging, staging.numel(), side)
+                skv.resume(resume_segs[j], skv.PARK_STAGED, staging, staging.numel(), side)
+        p1.record(side)
         for st in set(source_stream.values()) if per_source else ():
             stream.wait_stream(st)
         h1.record(stream)
