@@ -174,9 +174,10 @@ SKV_API int skv_resume(const skv_segment* segs, int n_segs, int mode, void* stag
 
 /* Chained copy (no reference counterpart: the pipelined relay of a one-to-many handoff).  Like skv_copy with
  * the TMA engine, but segment c is chunk c of a pipeline: no byte of chunk c is read before
- * wait_flags[c] >= value (this device's memory; bounded by timeout_ns of device time, 0 = 2 s), and once every
- * byte of chunk c has landed, value is stored to signal_flags[c] (any device's memory, e.g. the next GPU's
- * flags through CUDA IPC) with system-scope release semantics - while later chunks are still moving.  Either
+ * wait_flags[c] >= value (this device's memory; bounded by timeout_ns of device time, 0 = 2 s, at most 60 s),
+ * and once every byte of chunk c has landed, value is stored to signal_flags[c] (any device's memory, e.g. the
+ * next GPU's flags through CUDA IPC) with system-scope release semantics - while later chunks are still
+ * moving.  A destination may be a peer's memory too (the pushed form of a chain).  Either
  * flag array may be NULL.  Every chunk must be non-empty.  A wait that runs out sets SKV_STATUS_WAIT_TIMEOUT,
  * stops new reads, and leaves the unfinished chunks unsignalled.  One chained copy in flight per device (the
  * per-chunk counters are per device). */

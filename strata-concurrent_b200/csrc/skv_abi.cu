@@ -32,6 +32,24 @@ uint64_t splitmix64(uint64_t x) {
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 }  // namespace
 
+/// Makes `device` the calling thread's current device for a scope and gives the caller's device back after it.
+/// `error` is the failure of the switch (an ordinal that does not exist), with nothing switched.
+struct DeviceScope {
+    int prev = -1;
+    cudaError_t error = cudaSuccess;
+    explicit DeviceScope(int device) {
+        error = cudaGetDevice(&prev);
+        if (error != cudaSuccess) prev = -1;
+        else if (prev != device) error = cudaSetDevice(device);
+        if (error != cudaSuccess) (void) cudaGetLastError();
+    }
+    ~DeviceScope() {
+        if (prev >= 0) (void) cudaSetDevice(prev);
+    }
+    DeviceScope(const DeviceScope&) = delete;
+    DeviceScope& operator=(const DeviceScope&) = delete;
+};
+
 void set_error(const std::string& message) { t_error = message; }
 
 Tuning tuning() {
@@ -205,16 +223,16 @@ int skv_pool_create(int device, int64_t n_blocks, uint64_t block_bytes, skv_pool
     if (n_blocks <= 0 || n_blocks > INT32_MAX || block_bytes == 0 || block_bytes % 1024)
         return fail(SKV_EINVAL, "skv_pool_create: n_blocks in [1, 2^31) and block_bytes a positive multiple of 1 KiB");
     if ((uint64_t) n_blocks > UINT64_MAX / block_bytes) return fail(SKV_ERANGE, "skv_pool_create: pool size overflows");
-    int prev = -1;
-    cudaError_t e = cudaGetDevice(&prev);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
-    if ((e = cudaSetDevice(device)) != cudaSuccess) return cuda_fail(e, "cudaSetDevice");
     auto pool = std::make_unique<skv_pool>();
     pool->device = device;
     pool->block_bytes = block_bytes;
     pool->n_blocks = n_blocks;
-    e = cudaMalloc(&pool->base, (size_t) n_blocks * block_bytes);
-    cudaSetDevice(prev);
+    cudaError_t e;
+    {
+        DeviceScope on(device);
+        if (on.error != cudaSuccess) return cuda_fail(on.error, "skv_pool_create: cudaSetDevice");
+        e = cudaMalloc(&pool->base, (size_t) n_blocks * block_bytes);
+    }
     if (e != cudaSuccess) {
         (void) cudaGetLastError();
         return fail(SKV_ENOMEM, std::string("skv_pool_create: cudaMalloc: ") + cudaGetErrorString(e));
@@ -254,11 +272,11 @@ int skv_pool_destroy(skv_pool* pool) {
         delete pool;
         return SKV_OK;
     }
-    int prev = -1;
-    cudaGetDevice(&prev);
-    cudaSetDevice(pool->device);
-    const cudaError_t e = cudaFree(pool->base);
-    cudaSetDevice(prev);
+    cudaError_t e;
+    {
+        DeviceScope on(pool->device);
+        e = on.error != cudaSuccess ? on.error : cudaFree(pool->base);
+    }
     delete pool;
     return e == cudaSuccess ? SKV_OK : cuda_fail(e, "skv_pool_destroy: cudaFree");
 }
@@ -353,6 +371,7 @@ int skv_copy_chained(const skv_segment* segs, int n_segs, const uint64_t* wait_f
         if (segs[i].bytes == 0) return fail(SKV_EINVAL, "skv_copy_chained: every chunk must move at least one byte");
     if ((reinterpret_cast<uintptr_t>(wait_flags) | reinterpret_cast<uintptr_t>(signal_flags)) & 7u)
         return fail(SKV_EINVAL, "skv_copy_chained: flags must be 8-byte aligned");
+    if (timeout_ns > 60ull * 1000000000ull) return fail(SKV_EINVAL, "skv_copy_chained: timeout must be at most 60 s");
     CopyPlan plan;
     uint64_t tiles = 0;
     if (const int rc = build_plan(segs, n_segs, SKV_COPY_TMA, plan, tiles)) return rc;
@@ -394,9 +413,8 @@ int skv_get_copy_tuning(int* tma_stages, uint32_t* tma_tile_bytes, int* tma_ctas
 
 int skv_query_status(int device, void* stream, uint32_t* out_status) {
     if (!out_status) return fail(SKV_EINVAL, "skv_query_status: null output");
-    int prev = -1;
-    cudaGetDevice(&prev);
-    cudaSetDevice(device);
+    DeviceScope on(device);
+    if (on.error != cudaSuccess) return cuda_fail(on.error, "skv_query_status: cudaSetDevice");
     DeviceCtx* ctx = current_ctx();
     int rc = SKV_OK;
     if (!ctx) rc = SKV_ECUDA;
@@ -405,14 +423,12 @@ int skv_query_status(int device, void* stream, uint32_t* out_status) {
         if (e == cudaSuccess) e = cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
         if (e != cudaSuccess) rc = cuda_fail(e, "skv_query_status");
     }
-    cudaSetDevice(prev);
     return rc;
 }
 
 int skv_clear_status(int device, void* stream) {
-    int prev = -1;
-    cudaGetDevice(&prev);
-    cudaSetDevice(device);
+    DeviceScope on(device);
+    if (on.error != cudaSuccess) return cuda_fail(on.error, "skv_clear_status: cudaSetDevice");
     DeviceCtx* ctx = current_ctx();
     int rc = SKV_OK;
     if (!ctx) rc = SKV_ECUDA;
@@ -420,7 +436,6 @@ int skv_clear_status(int device, void* stream) {
         const cudaError_t e = cudaMemsetAsync(ctx->status, 0, 4, static_cast<cudaStream_t>(stream));
         if (e != cudaSuccess) rc = cuda_fail(e, "skv_clear_status");
     }
-    cudaSetDevice(prev);
     return rc;
 }
 
@@ -523,11 +538,10 @@ int skv_enable_peer(int device, int peer) {
     cudaError_t e = cudaDeviceCanAccessPeer(&can, device, peer);
     if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceCanAccessPeer");
     if (!can) return fail(SKV_EINVAL, "skv_enable_peer: the devices cannot access each other");
-    int prev = -1;
-    cudaGetDevice(&prev);
-    cudaSetDevice(device);
-    e = cudaDeviceEnablePeerAccess(peer, 0);
-    cudaSetDevice(prev);
+    {
+        DeviceScope on(device);
+        e = on.error != cudaSuccess ? on.error : cudaDeviceEnablePeerAccess(peer, 0);
+    }
     if (e == cudaErrorPeerAccessAlreadyEnabled) {
         (void) cudaGetLastError();
         return SKV_OK;
@@ -549,11 +563,10 @@ int skv_ipc_import(int device, const uint8_t handle[64], void** out_ptr) {
     if (!handle || !out_ptr) return fail(SKV_EINVAL, "skv_ipc_import: bad arguments");
     cudaIpcMemHandle_t h;
     std::memcpy(&h, handle, 64);
-    int prev = -1;
-    cudaGetDevice(&prev);
-    cudaSetDevice(device);
+    *out_ptr = nullptr;
+    DeviceScope on(device);
+    if (on.error != cudaSuccess) return cuda_fail(on.error, "skv_ipc_import: cudaSetDevice");
     const cudaError_t e = cudaIpcOpenMemHandle(out_ptr, h, cudaIpcMemLazyEnablePeerAccess);
-    cudaSetDevice(prev);
     return e == cudaSuccess ? SKV_OK : cuda_fail(e, "cudaIpcOpenMemHandle");
 }
 
