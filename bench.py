@@ -359,25 +359,51 @@ def e2e_park_resume(torch, kg, src: SeqOnGpu, dst: SeqOnGpu, steps: int, warmup:
     return out
 
 
-def cpu_baseline(tokens: int) -> dict | None:
-    """The reference's own host park/resume on ONE host core, bounded sample (a few reps of one sequence)."""
+def host_info() -> dict:
+    """The host the CPU arms ran on: its CPU model and how many cores it offers this process."""
+    model = None
+    try:
+        with open("/proc/cpuinfo") as f:
+            model = next((ln.split(":", 1)[1].strip() for ln in f if ln.startswith("model name")), None)
+    except OSError:
+        pass
+    try:
+        usable = len(os.sched_getaffinity(0))
+    except (AttributeError, OSError):
+        usable = os.cpu_count()
+    return {"cpu_model": model, "cores_total": os.cpu_count(), "cores_usable": usable}
+
+
+def cpu_baseline(tokens: int, reps: int = 20) -> dict | None:
+    """The reference's own host park/resume on ONE host core (this thread pinned to one core for the run), a
+    bounded sample: `reps` park + resume round trips of one sequence, median and p50/p99."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     try:
         import oracle as O
     except Exception:
         return None
     g = O.Geometry()
-    if O.ref_available():
-        src, dst, ids = reference_pools(O, g, tokens)
-        reps = 4
+    if not O.ref_available():
+        return None
+    src, dst, ids = reference_pools(O, g, tokens)
+    try:
+        before = os.sched_getaffinity(0)
+        os.sched_setaffinity(0, {min(before)})
+    except (AttributeError, OSError):
+        before = None
+    try:
         save, restore = O.ref_time_park_resume(src, dst, ids, reps)
-        t = (save + restore) / 1e3
-        b = O.metric_bytes(g, tokens)
-        return {"value": round(float(b / np.median(t) / 1e9), 3), "unit": UNIT, "cores": 1, "kind": "reference",
-                "sample": f"{reps} x conversation_snapshot_save+_restore of one {tokens}-token sequence "
-                          f"(reference sources, host pools), median", "save_ms": round(float(np.median(save)), 2),
-                "restore_ms": round(float(np.median(restore)), 2)}
-    return None
+    finally:
+        if before is not None:
+            os.sched_setaffinity(0, before)
+    t = save + restore
+    b = O.metric_bytes(g, tokens)
+    return {"value": round(float(b / (np.median(t) / 1e3) / 1e9), 3), "unit": UNIT, "cores": 1, "kind": "reference",
+            "sample": f"{reps} x conversation_snapshot_save+_restore of one {tokens}-token sequence (reference "
+                      f"sources, host pools) on one pinned core, median",
+            "save_ms": round(float(np.median(save)), 2), "restore_ms": round(float(np.median(restore)), 2),
+            "p50_ms": round(float(np.percentile(t, 50)), 2), "p99_ms": round(float(np.percentile(t, 99)), 2),
+            "pinned": before is not None, "host": host_info()}
 
 
 def reference_pools(O, g, tokens: int):
@@ -447,7 +473,7 @@ def run_reference(args) -> None:
                                             "tokens": args.tokens, "threads": threads},
             "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": threads, "kind": "reference",
                              "sample": f"{threads} threads x {per_step} conversation_snapshot_save+_restore each, "
-                                       f"wall {wall:.1f} s"},
+                                       f"wall {wall:.1f} s", "host": host_info()},
             "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line))
 
