@@ -1122,6 +1122,25 @@ def phased_schedule(plan: dict, sizes: list, world: int) -> dict:
     return {"bound_bytes": M, "phases": phases, "runs": runs}
 
 
+def phase_runs(rank: int, plan: dict, sizes: list, segs_of: dict, world: int) -> list:
+    """Decode GPU `rank`'s share of phased_schedule, ready to launch.  `sizes[i]` = sequence i's bytes (all 64,
+    for the global schedule); `segs_of[i]` = the segments moving sequence i into this GPU (each sequence it
+    receives; their bytes must add up to sizes[i]).  Each run gets `pieces` (its byte range of its flow, sliced
+    page-granular), `starts` / `ends` (the sequences whose first / last byte it moves).  A flow's sequences go
+    shortest first: the cuts are by bytes, so the order moves no phase, and most sequences land early."""
+    for i, segs in segs_of.items():
+        if sum(g.bytes for g in segs) != sizes[i]:
+            raise ValueError(f"sequence {i}: its segments move {sum(g.bytes for g in segs)} bytes, not {sizes[i]}")
+    out = []
+    for run in phased_schedule(plan, sizes, world)["runs"][rank]:
+        flow = sorted((i for i in segs_of if plan["owner"][i] == run["src"]), key=lambda i: (plan["lengths"][i], i))
+        ends = np.cumsum([sizes[i] for i in flow])
+        out.append(dict(run, pieces=skv.slice_segments([g for i in flow for g in segs_of[i]], run["lo"], run["hi"]),
+                        starts=[i for i, e in zip(flow, ends) if run["lo"] <= e - sizes[i] < run["hi"]],
+                        ends=[i for i, e in zip(flow, ends) if run["lo"] < e <= run["hi"]]))
+    return out
+
+
 def port_bound(plan: dict, sizes: list, world: int) -> dict:
     """Config 5's schedule-independent bound: the busiest NVLink port's bytes at the measured peer-copy rate."""
     m = phased_schedule(plan, sizes, world)["bound_bytes"]
@@ -1236,21 +1255,13 @@ def run_mixed(args, torch) -> dict | None:
     if decode and phased:
         stream_bytes = lambda t: (2 * kg.n_qsa * kg.pages(t) * kg.page_bytes + kg.gdn_bytes  # noqa: E731
                                   + 16 * ((4 * t + 15) // 16))
-        assert all(sum(g.bytes for g in segs_of[i]) == stream_bytes(lengths[i]) for i in mine_in)
-        sched = phased_schedule(plan, [stream_bytes(t) for t in lengths], world)
-        for run in sched["runs"][rank]:
-            # a flow's sequences shortest first: the cuts are by bytes, so the order moves no phase, and most
-            # sequences land early
-            flow = sorted((i for i in mine_in if owner[i] == run["src"]), key=lambda i: (lengths[i], i))
-            ends = np.cumsum([stream_bytes(lengths[i]) for i in flow])
-            pieces = skv.slice_segments([g for i in flow for g in segs_of[i]], run["lo"], run["hi"])
+        for run in phase_runs(rank, plan, [stream_bytes(t) for t in lengths], segs_of, world):
+            pieces = run["pieces"]
             arrays = [((skv.Segment * len(pieces[a:a + skv.MAX_SEGMENTS]))(*pieces[a:a + skv.MAX_SEGMENTS]),
                        len(pieces[a:a + skv.MAX_SEGMENTS])) for a in range(0, len(pieces), skv.MAX_SEGMENTS)]
             if run["signal"] and run["signal"][0] not in peer_flags:
                 peer_flags[run["signal"][0]] = skv.ipc_import(local, infos[run["signal"][0]]["flags"])
-            runs.append(dict(run, arrays=arrays,
-                             starts=[i for i, e in zip(flow, ends) if run["lo"] <= e - stream_bytes(lengths[i]) < run["hi"]],
-                             ends=[i for i, e in zip(flow, ends) if run["lo"] < e <= run["hi"]]))
+            runs.append(dict(run, arrays=arrays))
     side = torch.cuda.Stream()
     per_source = args.mixed_order == "per-source"
     source_stream = {p: torch.cuda.Stream() for p in sorted(set(owner[i] for i in mine_in))}

@@ -191,3 +191,71 @@ def test_two_rank_exchange_and_reductions():
     assert out[0][1] == out[1][1] == 11.0
     assert out[0][2] == [2.0, 2.0, 3.0]
     assert out[0][3] == pytest.approx(1 * 1000 * 3 / 0.011 / 1e9)
+
+
+def _fake_sequence_segments(kg, i, tokens):
+    """Segments shaped like one pulled sequence (paged K/V per layer, contiguous GDN rows and ids) with made-up,
+    distinct addresses: enough for the host-side cutting, nothing is launched."""
+    n = kg.pages(tokens) * kg.page_bytes
+    base = (i + 1) << 40
+    segs = [skv.segment(base, base + (1 << 36), n, src_pages=base + (1 << 30) + 4096 * j,
+                        dst_pages=base + (1 << 31) + 4096 * j, page_bytes=kg.page_bytes, src_page_limit=1 << 20,
+                        dst_page_limit=1 << 20) for j in range(2 * kg.n_qsa)]
+    segs.append(skv.segment(base + (1 << 37), base + (1 << 38), kg.gdn_bytes))
+    segs.append(skv.segment(base + (1 << 39), base + (1 << 39) + (1 << 34), 16 * ((4 * tokens + 15) // 16)))
+    return segs
+
+
+def _merged(segs):
+    """A list of segments with every piece that continues the one before it (same bases, the next table entry or
+    the next address on each side) folded into it: pieces cut from one segment fold back into that segment."""
+    out = []
+    for g in segs:
+        unit = g.page_bytes if (g.src_pages or g.dst_pages) else 16
+        cur = [g.src, g.dst, g.src_pages, g.dst_pages, g.bytes, unit]
+        if out:
+            p = out[-1]
+            n = p[4] // p[5]
+            follows = (p[5] == unit and
+                       (p[2] and cur[2] == p[2] + 4 * n and cur[0] == p[0] or not p[2] and not cur[2] and cur[0] == (p[0] or 0) + p[4]) and
+                       (p[3] and cur[3] == p[3] + 4 * n and cur[1] == p[1] or not p[3] and not cur[3] and cur[1] == (p[1] or 0) + p[4]))
+            if follows:
+                p[4] += g.bytes
+                continue
+        out.append(cur)
+    return out
+
+
+@pytest.mark.parametrize("world,seed", [(8, 1), (8, 5), (4, 2)])
+def test_phase_runs_move_every_sequence_once_in_schedule_order(world, seed):
+    """What each decode GPU launches under the phased order: its runs' pieces, flow by flow, are exactly its
+    sequences' segments (shortest first), every byte once; every sequence starts and ends in one run."""
+    kg = skv.KvGeometry()
+    plan = bench.mixed_plan(world, seed)
+    sizes = [2 * kg.n_qsa * kg.pages(t) * kg.page_bytes + kg.gdn_bytes + 16 * ((4 * t + 15) // 16)
+             for t in plan["lengths"]]
+    for d in range(1, world, 2):
+        mine = [i for i in range(len(sizes)) if plan["target"][i] == d]
+        segs_of = {i: _fake_sequence_segments(kg, i, plan["lengths"][i]) for i in mine}
+        runs = bench.phase_runs(d, plan, sizes, segs_of, world)
+        for s in range(0, world, 2):
+            flow = sorted((i for i in mine if plan["owner"][i] == s), key=lambda i: (plan["lengths"][i], i))
+            want = _merged([seg for i in flow for seg in segs_of[i]])
+            got = _merged([seg for r in runs if r["src"] == s for seg in r["pieces"]])
+            assert got == want
+        starts = [i for r in runs for i in r["starts"]]
+        ends = [i for r in runs for i in r["ends"]]
+        assert sorted(starts) == sorted(mine) == sorted(ends)
+        where = {i: j for j, r in enumerate(runs) for i in r["ends"]}
+        assert all(min(j for j, r in enumerate(runs) if i in r["starts"]) <= where[i] for i in mine)
+
+
+def test_phase_runs_refuse_segments_that_disagree_with_the_sizes():
+    kg = skv.KvGeometry()
+    plan = bench.mixed_plan(4, 1)
+    sizes = [2 * kg.n_qsa * kg.pages(t) * kg.page_bytes + kg.gdn_bytes + 16 * ((4 * t + 15) // 16)
+             for t in plan["lengths"]]
+    i = next(i for i in range(len(sizes)) if plan["target"][i] == 1)
+    segs = _fake_sequence_segments(kg, i, plan["lengths"][i])[:-1]      # the ids segment left out
+    with pytest.raises(ValueError):
+        bench.phase_runs(1, plan, sizes, {i: segs}, 4)
