@@ -2,6 +2,8 @@
 
 handoff_device_cpu_test: the 256-byte device descriptor a hand-off slot carries on one node - round trip, every
 refusal, and its trip through a real HandoffArena slot (claim, write, publish, read, release).
+wire_fuzz_cpu_test: the SR4H decoders (full and shape) against damaged copies of the reference's own payloads,
+compiled from the sources with AddressSanitizer and UndefinedBehaviorSanitizer.
 """
 import os
 import subprocess
@@ -33,3 +35,25 @@ def test_device_descriptor_round_trip_refusals_and_slot():
                            env=dict(os.environ, CUDA_VISIBLE_DEVICES=""))
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
     assert "checks passed" in r.stdout
+
+
+def test_wire_decoders_refuse_damaged_payloads_without_a_bad_access():
+    os.makedirs(BIN, exist_ok=True)
+    out = os.path.join(BIN, "wire_fuzz_cpu_test")
+    host = os.path.join(PKG, "csrc", "host")
+    srcs = [os.path.join(SRC, "wire_fuzz_cpu_test.cpp"), os.path.join(host, "conversation_wire.cpp"),
+            os.path.join(host, "pinned.cpp")]
+    deps = srcs + [os.path.join(host, "wire_detail.hpp")] + [
+        os.path.join(ROOT, "include", "strata_kv", h) for h in ("conversation_wire.hpp", "conversation_cache.hpp",
+                                                                 "conversation_buffer.hpp")]
+    if not os.path.exists(out) or any(os.path.getmtime(d) > os.path.getmtime(out) for d in deps):
+        subprocess.run(["g++", "-std=c++20", "-O1", "-g", "-fsanitize=address,undefined",
+                        "-fno-sanitize-recover=undefined", "-fno-omit-frame-pointer", "-I", os.path.join(ROOT, "include"),
+                        "-I", host, "-I", f"{CUDA}/include", "-o", out, *srcs, "-L", f"{CUDA}/lib64", "-lcudart",
+                        f"-Wl,-rpath,{CUDA}/lib64"], check=True)
+    golden = os.path.join(ROOT, "tests", "golden")
+    payloads = [os.path.join(golden, f"ref_payload_T{t}.bin") for t in (1, 5, 257)]
+    r = subprocess.run([out, "3000", *payloads], capture_output=True, text=True, timeout=600,
+                       env=dict(os.environ, CUDA_VISIBLE_DEVICES="", ASAN_OPTIONS="protect_shadow_gap=0:detect_leaks=0"))
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
+    assert ", OK" in r.stdout
