@@ -11,6 +11,8 @@ check-and-exit suite; passing it means the drop-in behaves as the reference's ow
   handoff_arena_test        the hand-off table: on-disk layout, sizing, the claim/publish/release lifecycle,
                             dead and recycled owners, leases, refusals, cross-process readers, a >1 GiB slot and
                             an instance restart (268 checks; child processes, a tmpfs arena under /dev/shm)
+The host suites run a second time as asan_* builds: this build's host sources compiled into the program with
+AddressSanitizer and UndefinedBehaviorSanitizer, LeakSanitizer on at exit.
 """
 import os
 import subprocess
@@ -34,3 +36,20 @@ def test_reference_suite_passes_against_the_drop_in(name, expect):
                        env=dict(os.environ, CUDA_VISIBLE_DEVICES=""))
     assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-2000:]
     assert expect in r.stdout
+
+
+@pytest.mark.parametrize("name,expect", [("asan_conversation_cache_test", "4282 checks passed"),
+                                         ("asan_saved_conv_wire_test", "483 checks passed"),
+                                         ("asan_conversation_validation_test", "1323 host-only checks passed"),
+                                         ("asan_handoff_arena_test", "268 checks, OK")])
+def test_reference_suite_passes_under_the_sanitizers(name, expect):
+    path = os.path.join(BIN, name)
+    if not os.path.exists(path):
+        pytest.skip(f"{name} not built (the reference tree was not present at build time)")
+    r = subprocess.run([path], capture_output=True, text=True, timeout=600,
+                       env=dict(os.environ, CUDA_VISIBLE_DEVICES="",
+                                ASAN_OPTIONS="protect_shadow_gap=0:detect_leaks=1:abort_on_error=0",
+                                UBSAN_OPTIONS="print_stacktrace=1:halt_on_error=1"))
+    assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-4000:]
+    assert expect in r.stdout
+    assert "runtime error" not in r.stderr and "ERROR: AddressSanitizer" not in r.stderr
