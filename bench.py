@@ -34,6 +34,7 @@ import numpy as np
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.join(ROOT, "strata-concurrent_b200"))
 
+import handoff_schedule  # noqa: E402
 import skv  # noqa: E402
 
 METRIC = "KV handoff GB/s & p50/p99 ms per 32K-token sequence"
@@ -1054,98 +1055,38 @@ def mixed_plan(world: int, seed: int) -> dict:
             "target": [int(x) for x in rng.choice(decode, MIXED_SEQUENCES)]}
 
 
-def phased_schedule(plan: dict, sizes: list, world: int) -> dict:
-    """An order for config 5's pulls that keeps every NVLink port busy with ONE transfer at a time.
-
-    D[s][d] = the bytes prefill GPU s hands to decode GPU d.  No schedule ends before the busiest port (a prefill
-    GPU's egress or a decode GPU's ingress, M bytes) has carried its load.  Pad D with idle time to a matrix whose
-    rows and columns all sum to M, and split it (Birkhoff-von Neumann) into phases: in phase k every prefill GPU
-    feeds exactly one decode GPU for w_k bytes.  Each flow (s, d) - its sequences back to back, in an order the
-    caller picks - is cut at the phase boundaries, real bytes first, so a phase's share of a flow may end early
-    (idle padding).
-    Run as: every decode GPU pulls its phases in order on one stream; before pulling from s it waits until the
-    previous decode GPU that pulled from s is done (that GPU signals it).  Waits only point at earlier phases, so
-    no cycle; each port carries one transfer at a time, and the whole ends no later than M at the port rate.
-
-    Returns {"bound_bytes": M, "phases": [(perm, w)], "runs": {decode rank: [run]}}, a run being
-    {"phase", "src" (rank), "lo", "hi" (byte range of the flow src -> this decode GPU), "wait" (this GPU's flag
-    index or None), "signal" ((rank, flag index) or None)}; a decode GPU's flag index is its run index."""
-    import itertools
-    src_ranks = [r for r in range(world) if r % 2 == 0]
-    dst_ranks = [r for r in range(world) if r % 2 == 1]
-    n = len(dst_ranks)
-    D = np.zeros((n, n), dtype=np.int64)
+def mixed_demand(plan: dict, sizes: list) -> dict:
+    """Config 5's bytes per (prefill rank, decode rank)."""
+    demand = {}
     for i, (o, d) in enumerate(zip(plan["owner"], plan["target"])):
-        D[src_ranks.index(o), dst_ranks.index(d)] += int(sizes[i])
-    M = int(max(D.sum(1).max(), D.sum(0).max()))
-    P = D.copy()
-    rdef, cdef = M - P.sum(1), M - P.sum(0)
-    i = j = 0
-    while i < n and j < n:                       # north-west corner: pad rows and columns up to M
-        x = min(rdef[i], cdef[j])
-        P[i, j] += x
-        rdef[i] -= x
-        cdef[j] -= x
-        i += rdef[i] == 0
-        j += cdef[j] == 0
-    phases = []
-    perms = list(itertools.permutations(range(n)))
-    while P.any():                               # every row and column still sums to the same amount
-        w, perm = max((min(int(P[s, p[s]]) for s in range(n)), p) for p in perms)
-        if w <= 0:
-            raise RuntimeError("no positive permutation: the padded matrix is not balanced")
-        phases.append((perm, w))
-        for s in range(n):
-            P[s, perm[s]] -= w
-    left = D.copy()                              # real bytes still to place, per flow
-    cursor = np.zeros((n, n), dtype=np.int64)    # bytes of each flow already placed
-    runs = {d: [] for d in dst_ranks}
-    last = {}                                    # source rank -> (decode rank, run index) of its latest real run
-    for k, (perm, w) in enumerate(phases):
-        for s in range(n):
-            d = perm[s]
-            real = int(min(w, left[s, d]))
-            if real == 0:
-                continue
-            left[s, d] -= real
-            dr, sr = dst_ranks[d], src_ranks[s]
-            run = {"phase": k, "src": sr, "lo": int(cursor[s, d]), "hi": int(cursor[s, d]) + real,
-                   "wait": None, "signal": None}
-            cursor[s, d] += real
-            idx = len(runs[dr])
-            prev = last.get(sr)
-            if prev is not None and prev[0] != dr:
-                run["wait"] = idx
-                runs[prev[0]][prev[1]]["signal"] = (dr, idx)
-            runs[dr].append(run)
-            last[sr] = (dr, idx)
-    return {"bound_bytes": M, "phases": phases, "runs": runs}
+        demand[(o, d)] = demand.get((o, d), 0) + int(sizes[i])
+    return demand
+
+
+def phased_schedule(plan: dict, sizes: list, world: int) -> dict:
+    """Config 5's pulls in port-exclusive phases (handoff_schedule.schedule): prefill ranks (even) are the
+    sources, decode ranks (odd) the destinations."""
+    return handoff_schedule.schedule(mixed_demand(plan, sizes), [r for r in range(world) if r % 2 == 0],
+                                     [r for r in range(world) if r % 2 == 1])
 
 
 def phase_runs(rank: int, plan: dict, sizes: list, segs_of: dict, world: int) -> list:
-    """Decode GPU `rank`'s share of phased_schedule, ready to launch.  `sizes[i]` = sequence i's bytes (all 64,
-    for the global schedule); `segs_of[i]` = the segments moving sequence i into this GPU (each sequence it
-    receives; their bytes must add up to sizes[i]).  Each run gets `pieces` (its byte range of its flow, sliced
-    page-granular), `starts` / `ends` (the sequences whose first / last byte it moves).  A flow's sequences go
-    shortest first: the cuts are by bytes, so the order moves no phase, and most sequences land early."""
+    """Decode GPU `rank`'s runs under phased_schedule, ready to launch (handoff_schedule.launch_list).  `sizes[i]`
+    = sequence i's bytes (all 64, for the global schedule); `segs_of[i]` = the segments moving sequence i into this
+    GPU (each sequence it receives).  A flow's sequences go shortest first: the cuts are by bytes, so the order
+    moves no phase, and most sequences land early."""
     for i, segs in segs_of.items():
         if sum(g.bytes for g in segs) != sizes[i]:
             raise ValueError(f"sequence {i}: its segments move {sum(g.bytes for g in segs)} bytes, not {sizes[i]}")
-    out = []
-    for run in phased_schedule(plan, sizes, world)["runs"][rank]:
-        flow = sorted((i for i in segs_of if plan["owner"][i] == run["src"]), key=lambda i: (plan["lengths"][i], i))
-        ends = np.cumsum([sizes[i] for i in flow])
-        out.append(dict(run, pieces=skv.slice_segments([g for i in flow for g in segs_of[i]], run["lo"], run["hi"]),
-                        starts=[i for i, e in zip(flow, ends) if run["lo"] <= e - sizes[i] < run["hi"]],
-                        ends=[i for i, e in zip(flow, ends) if run["lo"] < e <= run["hi"]]))
-    return out
+    flows = {}
+    for i in sorted(segs_of, key=lambda i: (plan["lengths"][i], i)):
+        flows.setdefault(plan["owner"][i], []).append((i, segs_of[i]))
+    return handoff_schedule.launch_list(phased_schedule(plan, sizes, world), rank, flows)
 
 
 def port_bound(plan: dict, sizes: list, world: int) -> dict:
     """Config 5's schedule-independent bound: the busiest NVLink port's bytes at the measured peer-copy rate."""
-    m = phased_schedule(plan, sizes, world)["bound_bytes"]
-    ms = m / NVLINK_PEER_COPY_GBS / 1e6
-    return {"busiest_port_bytes": m, "ms": round(ms, 3), "gbs": round(sum(sizes) / ms / 1e6, 1)}
+    return handoff_schedule.port_bound(mixed_demand(plan, sizes), NVLINK_PEER_COPY_GBS)
 
 
 class SeqSet:
