@@ -201,6 +201,30 @@ SKV_API int skv_signal(uint64_t* flag, uint64_t value, void* stream);
  * timeout the wait ends and SKV_STATUS_WAIT_TIMEOUT is set (never a trap, never an endless loop). */
 SKV_API int skv_wait_flag(const uint64_t* flag, uint64_t value, uint64_t timeout_ns, void* stream);
 
+/* ------------------------------------------------------------------ many-to-many hand-off order
+ * No reference counterpart (its split roles move one conversation at a time through pinned RAM).  When several
+ * destination GPUs pull from several source GPUs at once, two destinations reading one source split its NVLink
+ * egress while another port idles.  skv_schedule_phases orders such a batch in port-exclusive phases: in each
+ * phase every source feeds at most one destination, and with equal port rates the batch ends when the busiest
+ * port (a row or column sum of `demand`) has carried its bytes - the bound for any order.
+ *
+ * demand: n_src x n_dst bytes, row-major (source s, destination d); 1 <= n_src, n_dst <= 64.  Destination d's
+ * runs are written at runs + d * max_runs, in the order to issue them, and their count to n_runs[d]; a
+ * destination's flag index is its run index.  max_runs >= n * n with n = max(n_src, n_dst) always suffices;
+ * fewer is refused with SKV_ERANGE if a destination needs more.  *bound_bytes = the busiest port's bytes,
+ * *n_phases = the number of phases.  Host-only: no device is touched. */
+typedef struct skv_sched_run {
+    int32_t phase;       /* phase index */
+    int32_t src;         /* the source it reads (row of demand) */
+    uint64_t lo, hi;     /* bytes [lo, hi) of the flow src -> this destination */
+    int32_t wait;        /* before the run: wait for this destination's flag `wait` (-1: none) */
+    int32_t signal_dst;  /* after the run: release flag signal_idx of destination signal_dst (-1: none) */
+    int32_t signal_idx;
+    int32_t reserved;
+} skv_sched_run;
+SKV_API int skv_schedule_phases(const uint64_t* demand, int n_src, int n_dst, skv_sched_run* runs, int max_runs,
+                                int* n_runs, uint64_t* bound_bytes, int* n_phases);
+
 #ifdef __cplusplus
 }
 #endif

@@ -22,7 +22,7 @@ CUDA_SOURCES = ["skv_copy.cu", "skv_abi.cu", "kv_stream.cu"]
 # the C++ drop-in layer (strata::core API), host code on top of the C ABI
 HOST_SOURCES = ["host/pinned.cpp", "host/transfer.cpp", "host/conversation_snapshot.cpp", "host/conversation_state.cpp",
                 "host/conversation_wire.cpp", "host/conversation_wire_device.cpp", "host/handoff.cpp",
-                "host/handoff_device.cpp"]
+                "host/handoff_device.cpp", "host/handoff_schedule.cpp"]
 CXX = os.environ.get("CXX", "g++")
 CXXFLAGS = ["-std=c++20", "-O2", "-fPIC", "-Wall", "-Wextra", "-Wno-unused-parameter", "-I", INCLUDE, "-I", CSRC,
             "-I", "/usr/local/cuda/include"]

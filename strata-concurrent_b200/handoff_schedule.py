@@ -9,7 +9,8 @@ that bound when every port moves at one rate:
 * pad D with idle time until every row and every column sums to M (north-west corner rule);
 * split the padded matrix into permutation phases (Birkhoff-von Neumann: a matrix whose rows and columns all
   have one sum always has a permutation of positive entries; take the one with the largest smallest entry and
-  subtract it); in phase k every source feeds exactly one destination for w_k bytes, and the w_k add up to M;
+  subtract it); in phase k every source feeds exactly one destination for w_k bytes, and the w_k add up to M
+  (native: skv_schedule_phases, csrc/host/handoff_schedule.cpp);
 * cut each flow (s, d) - the bytes s sends d, back to back - at its phases' boundaries, real bytes first, so a
   phase's share of a flow may end early (idle padding);
 * each destination runs its phases in order on one stream; before it reads a source that another destination
@@ -21,123 +22,44 @@ GB/s against 1,900-1,942 with every pair of GPUs transferring at once.
 """
 from __future__ import annotations
 
-import itertools
+import ctypes as C
 
 import numpy as np
 
 import skv
 
 
-def _pad(D: np.ndarray) -> tuple:
-    """The padded square matrix (every row and column summing to M) and M."""
-    n = D.shape[0]
-    M = int(max(D.sum(1).max(), D.sum(0).max())) if n else 0
-    P = D.copy()
-    rdef, cdef = M - P.sum(1), M - P.sum(0)
-    i = j = 0
-    while i < n and j < n:
-        x = min(rdef[i], cdef[j])
-        P[i, j] += x
-        rdef[i] -= x
-        cdef[j] -= x
-        i += rdef[i] == 0
-        j += cdef[j] == 0
-    return P, M
-
-
-def _perfect_matching(allowed: np.ndarray):
-    """A perfect matching of the bipartite graph `allowed` (rows -> columns) by augmenting paths, or None."""
-    n = allowed.shape[0]
-    match_col = [-1] * n
-
-    def augment(r, seen):
-        for c in range(n):
-            if allowed[r, c] and not seen[c]:
-                seen[c] = True
-                if match_col[c] < 0 or augment(match_col[c], seen):
-                    match_col[c] = r
-                    return True
-        return False
-
-    for r in range(n):
-        if not augment(r, [False] * n):
-            return None
-    perm = [0] * n
-    for c, r in enumerate(match_col):
-        perm[r] = c
-    return tuple(perm)
-
-
-def _bottleneck_permutation(P: np.ndarray) -> tuple:
-    """The permutation whose smallest entry is largest, and that entry.  Exhaustive (ties to the largest
-    permutation in lexicographic order) up to 6 x 6; above, a binary search over thresholds with matchings."""
-    n = P.shape[0]
-    if n <= 6:
-        w, perm = max((min(int(P[s, p[s]]) for s in range(n)), p) for p in itertools.permutations(range(n)))
-        return perm, w
-    values = np.unique(P[P > 0])
-    lo, hi, best = 0, len(values) - 1, None
-    while lo <= hi:
-        mid = (lo + hi) // 2
-        perm = _perfect_matching(P >= values[mid])
-        if perm is None:
-            hi = mid - 1
-        else:
-            best, lo = perm, mid + 1
-    if best is None:
-        return None, 0
-    return best, min(int(P[s, best[s]]) for s in range(n))
-
-
 def schedule(demand: dict, sources: list | None = None, destinations: list | None = None) -> dict:
-    """The port-exclusive order of a batch of hand-offs.
+    """The port-exclusive order of a batch of hand-offs (skv_schedule_phases in libstrata_kv.so).
 
     `demand` maps (source, destination) to bytes; `sources` and `destinations` fix the order of the matrix's rows
-    and columns (default: sorted).  Returns {"bound_bytes": M, "phases": [(perm, w)], "runs": {destination:
-    [run]}}: perm maps source index -> destination index (indices past the given lists are idle padding), and a
-    run is {"phase", "src", "lo", "hi" (its byte range of the flow src -> destination), "wait" (this
-    destination's flag index, or None), "signal" ((destination, flag index) to release after the run, or None)};
-    a destination's flag index is its run index."""
+    and columns (default: sorted).  Returns {"bound_bytes": M, "n_phases": P, "runs": {destination: [run]}}, a run
+    being {"phase", "src", "lo", "hi" (its byte range of the flow src -> destination), "wait" (this destination's
+    flag index, or None), "signal" ((destination, flag index) to release after the run, or None)}; a
+    destination's flag index is its run index."""
     sources = list(sources) if sources is not None else sorted({s for s, _ in demand})
     destinations = list(destinations) if destinations is not None else sorted({d for _, d in demand})
-    n = max(len(sources), len(destinations))
-    D = np.zeros((n, n), dtype=np.int64)
+    ns, nd = len(sources), len(destinations)
+    D = np.zeros((ns, nd), dtype=np.uint64)
     for (s, d), b in demand.items():
         if b < 0:
             raise ValueError("a flow cannot move a negative number of bytes")
-        D[sources.index(s), destinations.index(d)] += int(b)
-    P, M = _pad(D)
-    phases = []
-    while P.any():
-        perm, w = _bottleneck_permutation(P)
-        if w <= 0:
-            raise RuntimeError("no positive permutation: the padded matrix is not balanced")
-        phases.append((perm, w))
-        for s in range(n):
-            P[s, perm[s]] -= w
-    left = D.copy()
-    cursor = np.zeros((n, n), dtype=np.int64)
-    runs = {d: [] for d in destinations}
-    last = {}                                    # source -> (destination, run index) of its latest real run
-    for k, (perm, w) in enumerate(phases):
-        for s in range(n):
-            d = perm[s]
-            real = int(min(w, left[s, d]))
-            if real == 0:
-                continue
-            left[s, d] -= real
-            dst, src = destinations[d], sources[s]
-            run = {"phase": k, "src": src, "lo": int(cursor[s, d]), "hi": int(cursor[s, d]) + real,
-                   "wait": None, "signal": None}
-            cursor[s, d] += real
-            idx = len(runs[dst])
-            prev = last.get(src)
-            if prev is not None and prev[0] != dst:
-                run["wait"] = idx
-                runs[prev[0]][prev[1]]["signal"] = (dst, idx)
-            runs[dst].append(run)
-            last[src] = (dst, idx)
-    return {"bound_bytes": M, "phases": phases, "runs": runs}
+        D[sources.index(s), destinations.index(d)] += np.uint64(b)
+    n = max(ns, nd)
+    max_runs = n * n
+    runs = (skv.SchedRun * (nd * max_runs))()
+    n_runs = np.zeros(nd, dtype=np.int32)
+    bound = C.c_uint64()
+    phases = C.c_int()
+    skv.check(skv.lib().skv_schedule_phases(D.ctypes.data, ns, nd, runs, max_runs, n_runs.ctypes.data,
+                                            C.byref(bound), C.byref(phases)))
+    out = {}
+    for d in range(nd):
+        out[destinations[d]] = [{"phase": r.phase, "src": sources[r.src], "lo": int(r.lo), "hi": int(r.hi),
+                                 "wait": None if r.wait < 0 else r.wait,
+                                 "signal": None if r.signal_dst < 0 else (destinations[r.signal_dst], r.signal_idx)}
+                                for r in runs[d * max_runs:d * max_runs + int(n_runs[d])]]
+    return {"bound_bytes": int(bound.value), "n_phases": int(phases.value), "runs": out}
 
 
 def launch_list(sched: dict, destination, flows: dict) -> list:

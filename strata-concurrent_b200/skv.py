@@ -46,6 +46,12 @@ class Segment(C.Structure):
                 ("src_page_limit", C.c_int64), ("dst_page_limit", C.c_int64)]
 
 
+class SchedRun(C.Structure):
+    """skv_sched_run: one transfer of a many-to-many hand-off batch (skv_schedule_phases)."""
+    _fields_ = [("phase", C.c_int32), ("src", C.c_int32), ("lo", C.c_uint64), ("hi", C.c_uint64),
+                ("wait", C.c_int32), ("signal_dst", C.c_int32), ("signal_idx", C.c_int32), ("reserved", C.c_int32)]
+
+
 _lib = None
 
 _SIGNATURES = {
@@ -82,6 +88,8 @@ _SIGNATURES = {
     "skv_ipc_close": ([C.c_void_p], C.c_int),
     "skv_signal": ([C.c_void_p, C.c_uint64, C.c_void_p], C.c_int),
     "skv_wait_flag": ([C.c_void_p, C.c_uint64, C.c_uint64, C.c_void_p], C.c_int),
+    "skv_schedule_phases": ([C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_int, C.c_void_p, C.POINTER(C.c_uint64),
+                             C.POINTER(C.c_int)], C.c_int),
 }
 
 

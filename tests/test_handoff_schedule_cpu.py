@@ -1,4 +1,5 @@
-"""handoff_schedule: the port-exclusive order of many-to-many hand-offs (host-side policy), on CPU.
+"""handoff_schedule / skv_schedule_phases: the port-exclusive order of many-to-many hand-offs (host-side policy),
+on CPU, checked run for run against the Python restatement in tests/sched_restatement.py.
 
 For any demand matrix - square or not, small (exhaustive permutation search) or large (bottleneck matchings) -
 the phases add up to the busiest port's bytes, no source or destination carries two transfers in one phase,
@@ -9,21 +10,25 @@ import numpy as np
 import pytest
 
 import handoff_schedule as hs
+import sched_restatement
 import skv
 from test_pairs_cpu import _play
 
 
 def _check(demand, sched):
+    ref = sched_restatement.schedule(demand)
+    assert ref["runs"] == sched["runs"] and ref["bound_bytes"] == sched["bound_bytes"]
+    assert len(ref["phases"]) == sched["n_phases"]
     rows, cols = {}, {}
     for (s, d), b in demand.items():
         rows[s] = rows.get(s, 0) + b
         cols[d] = cols.get(d, 0) + b
     M = max(list(rows.values()) + list(cols.values()))
     assert sched["bound_bytes"] == M
-    assert sum(w for _, w in sched["phases"]) == M
-    for perm, _ in sched["phases"]:
+    assert sum(w for _, w in ref["phases"]) == M
+    for perm, _ in ref["phases"]:
         assert sorted(perm) == list(range(len(perm)))
-    for k in range(len(sched["phases"])):
+    for k in range(sched["n_phases"]):
         used = [(r["src"], d) for d, rs in sched["runs"].items() for r in rs if r["phase"] == k]
         assert len({s for s, _ in used}) == len(used) and len({d for _, d in used}) == len(used)
     for (s, d), b in demand.items():
@@ -57,7 +62,7 @@ def test_schedule_meets_the_port_bound(n_src, n_dst, seed):
 def test_one_hot_demand_is_one_phase():
     demand = {(0, 1): 100, (2, 3): 100}
     sched = hs.schedule(demand)
-    assert len(sched["phases"]) == 1
+    assert sched["n_phases"] == 1
     assert all(r["wait"] is None and r["signal"] is None for rs in sched["runs"].values() for r in rs)
 
 
@@ -79,3 +84,34 @@ def test_port_bound():
     b = hs.port_bound({(0, 1): 300, (0, 3): 200, (2, 3): 400}, 100.0)
     assert b["busiest_port_bytes"] == 600          # destination 3's ingress
     assert b["ms"] == pytest.approx(600 / 100.0 / 1e6, abs=1e-3)
+
+
+def test_native_schedule_equals_the_restatement_on_random_batches():
+    rng = np.random.default_rng(11)
+    for trial in range(300):
+        ns, nd = int(rng.integers(1, 10)), int(rng.integers(1, 10))
+        demand = {(s, d): int(rng.integers(0, 1 << int(rng.integers(1, 40))))
+                  for s in range(ns) for d in range(nd) if rng.random() < 0.6}
+        if not any(demand.values()):
+            continue
+        got, ref = hs.schedule(demand), sched_restatement.schedule(demand)
+        assert got["runs"] == ref["runs"] and got["bound_bytes"] == ref["bound_bytes"], trial
+        assert got["n_phases"] == len(ref["phases"])
+
+
+def test_native_schedule_refuses_bad_arguments():
+    import ctypes as C
+    L = skv.lib()
+    runs = (skv.SchedRun * 4)()
+    n_runs = (C.c_int * 2)()
+    bound, phases = C.c_uint64(), C.c_int()
+    demand = (C.c_uint64 * 4)(5, 0, 0, 5)
+    assert L.skv_schedule_phases(demand, 0, 2, runs, 2, n_runs, C.byref(bound), C.byref(phases)) == skv.EINVAL
+    assert L.skv_schedule_phases(demand, 2, 2, None, 2, n_runs, C.byref(bound), C.byref(phases)) == skv.EINVAL
+    huge = (C.c_uint64 * 4)(1 << 62, 0, 0, 1)
+    assert L.skv_schedule_phases(huge, 2, 2, runs, 2, n_runs, C.byref(bound), C.byref(phases)) == skv.ERANGE
+    # destination 0 reads two sources, so it needs two runs; room for one is refused
+    crowded = (C.c_uint64 * 4)(3, 0, 4, 0)
+    assert L.skv_schedule_phases(crowded, 2, 2, runs, 1, n_runs, C.byref(bound), C.byref(phases)) == skv.ERANGE
+    assert L.skv_schedule_phases(demand, 2, 2, runs, 2, n_runs, C.byref(bound), C.byref(phases)) == skv.OK
+    assert bound.value == 5 and phases.value == 1 and list(n_runs) == [1, 1]

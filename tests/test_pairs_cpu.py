@@ -11,6 +11,7 @@ import torch.distributed as dist
 import torch.multiprocessing as mp
 
 import bench
+import sched_restatement
 import skv
 
 
@@ -101,9 +102,14 @@ def test_phased_schedule_tiles_every_flow_and_meets_the_port_bound(world, seed):
     egress = {s: sum(b for b, o in zip(sizes, plan["owner"]) if o == s) for s in range(0, world, 2)}
     ingress = {d: sum(b for b, t in zip(sizes, plan["target"]) if t == d) for d in range(1, world, 2)}
     assert sched["bound_bytes"] == max(max(egress.values()), max(ingress.values()))
-    # phases are permutations whose weights sum to the bound
-    assert sum(w for _, w in sched["phases"]) == sched["bound_bytes"]
-    assert all(sorted(p) == list(range(world // 2)) for p, _ in sched["phases"])
+    # the native schedule equals the Python restatement run for run; its phases are permutations whose
+    # weights sum to the bound
+    ref = sched_restatement.schedule(bench.mixed_demand(plan, sizes), list(range(0, world, 2)),
+                                     list(range(1, world, 2)))
+    assert ref["runs"] == sched["runs"] and ref["bound_bytes"] == sched["bound_bytes"]
+    assert len(ref["phases"]) == sched["n_phases"]
+    assert sum(w for _, w in ref["phases"]) == sched["bound_bytes"]
+    assert all(sorted(p) == list(range(world // 2)) for p, _ in ref["phases"])
     # every flow (src -> dst) is cut into consecutive byte ranges covering exactly its sequences
     for d, rs in sched["runs"].items():
         assert [r["phase"] for r in rs] == sorted(r["phase"] for r in rs)
@@ -116,7 +122,7 @@ def test_phased_schedule_tiles_every_flow_and_meets_the_port_bound(world, seed):
                 pos = r["hi"]
             assert pos == want
     # in each phase a source feeds at most one decode GPU; reads of one source are chained by signals
-    for k in range(len(sched["phases"])):
+    for k in range(sched["n_phases"]):
         srcs = [r["src"] for rs in sched["runs"].values() for r in rs if r["phase"] == k]
         assert len(srcs) == len(set(srcs))
     # with every port at one rate, the order ends exactly at the port bound (and never deadlocks)
