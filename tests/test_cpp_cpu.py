@@ -4,6 +4,8 @@ handoff_device_cpu_test: the 256-byte device descriptor a hand-off slot carries 
 refusal, and its trip through a real HandoffArena slot (claim, write, publish, read, release).
 wire_fuzz_cpu_test: the SR4H decoders (full and shape) against damaged copies of the reference's own payloads,
 compiled from the sources with AddressSanitizer and UndefinedBehaviorSanitizer.
+c_abi_cpu_test: include/strata_kv.h compiled as pedantic C99 with warnings as errors, and the entry points that
+need no GPU called from C.
 """
 import os
 import subprocess
@@ -55,5 +57,17 @@ def test_wire_decoders_refuse_damaged_payloads_without_a_bad_access():
     payloads = [os.path.join(golden, f"ref_payload_T{t}.bin") for t in (1, 5, 257)]
     r = subprocess.run([out, "3000", *payloads], capture_output=True, text=True, timeout=600,
                        env=dict(os.environ, CUDA_VISIBLE_DEVICES="", ASAN_OPTIONS="protect_shadow_gap=0:detect_leaks=0"))
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
+    assert ", OK" in r.stdout
+
+
+def test_the_c_header_is_c_and_the_host_entry_points_work_from_c():
+    os.makedirs(BIN, exist_ok=True)
+    src = os.path.join(SRC, "c_abi_cpu_test.c")
+    out = os.path.join(BIN, "c_abi_cpu_test")
+    subprocess.run(["gcc", "-std=c99", "-Wall", "-Wextra", "-pedantic", "-Werror", "-I", os.path.join(ROOT, "include"),
+                    "-o", out, src, "-L", PKG, "-lstrata_kv", f"-Wl,-rpath,{PKG}", "-L", f"{CUDA}/lib64", "-lcudart",
+                    f"-Wl,-rpath,{CUDA}/lib64"], check=True)
+    r = subprocess.run([out], capture_output=True, text=True, timeout=120, env=dict(os.environ, CUDA_VISIBLE_DEVICES=""))
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
     assert ", OK" in r.stdout
