@@ -71,3 +71,20 @@ def test_the_c_header_is_c_and_the_host_entry_points_work_from_c():
     r = subprocess.run([out], capture_output=True, text=True, timeout=120, env=dict(os.environ, CUDA_VISIBLE_DEVICES=""))
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
     assert ", OK" in r.stdout
+
+
+def test_every_cxx_header_stands_alone_and_compiles_clean():
+    """Each include/strata_kv/*.hpp compiles as the only include of a translation unit (twice, for the guard) with
+    -Wall -Wextra -Wpedantic -Wshadow -Werror: what a maintainer's target includes needs nothing else first."""
+    hdr_dir = os.path.join(ROOT, "include", "strata_kv")
+    names = sorted(n for n in os.listdir(hdr_dir) if n.endswith(".hpp"))
+    assert names
+    with tempfile.TemporaryDirectory() as d:
+        for n in names:
+            tu = os.path.join(d, "tu.cpp")
+            with open(tu, "w") as f:
+                f.write(f'#include "strata_kv/{n}"\n#include "strata_kv/{n}"\n')
+            r = subprocess.run(["g++", "-std=c++20", "-Wall", "-Wextra", "-Wpedantic", "-Wshadow", "-Werror",
+                                "-fsyntax-only", "-I", os.path.join(ROOT, "include"), "-I", f"{CUDA}/include", tu],
+                               capture_output=True, text=True, timeout=120)
+            assert r.returncode == 0, n + ": " + r.stderr[-2000:]
