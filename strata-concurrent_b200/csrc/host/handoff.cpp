@@ -87,6 +87,26 @@ bool slot_header_sane(const HandoffSlotHeader& h) {
            h.header_bytes == kHandoffHeaderBytes;
 }
 
+/// Why an arena header's tier table cannot describe its file, or "" when it can: the tiers lie back to back from
+/// byte 4096 in order, each count x (4096-byte header + slot bytes) without overflow, the slot counts add up to
+/// slot_total (an int slot index reaches them all), and the last tier ends at arena_bytes.  A reader checks this
+/// before it computes any slot address from the header of a file another process wrote.
+std::string tier_layout_error(const HandoffArenaHeader& h) {
+    uint64_t at = kHandoffHeaderBytes, slots = 0;
+    for (uint32_t t = 0; t < h.tier_count; ++t) {
+        if (h.tier_slot_off[t] != at) return "tier " + num(t) + " starts at byte " + num(h.tier_slot_off[t]) + ", not " + num(at);
+        uint64_t region = 0;
+        if (__builtin_add_overflow(h.tier_slot_bytes[t], kHandoffHeaderBytes, &region) ||
+            __builtin_mul_overflow(region, h.tier_slot_count[t], &region) || __builtin_add_overflow(at, region, &at) ||
+            __builtin_add_overflow(slots, h.tier_slot_count[t], &slots))
+            return "tier " + num(t) + "'s size overflows";
+    }
+    if (slots != h.slot_total) return "the tiers hold " + num(slots) + " slots, the header says " + num(h.slot_total);
+    if (slots > (uint64_t) INT32_MAX) return "more slots than an int index reaches";
+    if (at != h.arena_bytes) return "the tiers end at byte " + num(at) + ", the header says " + num(h.arena_bytes);
+    return {};
+}
+
 std::string tier_list(const uint64_t* v, uint32_t n) {
     std::string s;
     for (uint32_t i = 0; i < n; ++i) s += (i ? "," : "") + num(v[i]);
@@ -713,6 +733,10 @@ bool HandoffArena::open_reader(const std::string& path, uint64_t pack_hash, uint
     else if (ok && h.geom_hash != geom_hash)
         ok = fail(err, "geometry hash " + hex16(h.geom_hash) + " of " + path + " differs from this instance's " +
                            hex16(geom_hash));
+    else if (ok) {
+        const std::string why = tier_layout_error(h);
+        if (!why.empty()) ok = fail(err, path + " has an inconsistent tier table: " + why);
+    }
     if (!ok) {
         close_();
         return false;
@@ -751,6 +775,9 @@ bool HandoffArena::read_slot(int index, uint64_t expect_nonce, uint64_t client_i
         return fail(err, s + " declares " + num(h.payload_bytes) + " payload bytes in a " + num(cap) + "-byte slot");
     const uint64_t page = (uint64_t) ::sysconf(_SC_PAGESIZE);
     const uint64_t off = base + kHandoffHeaderBytes;
+    struct stat st{};
+    if (::fstat(fd_, &st) != 0 || (uint64_t) st.st_size < off + h.payload_bytes)
+        return fail(err, "the arena file is shorter than " + s + "'s payload");
     const uint64_t aligned = off & ~(page - 1);
     const uint64_t len = (off - aligned) + std::max<uint64_t>(h.payload_bytes, 1);
     void* map = ::mmap(nullptr, len, PROT_READ, MAP_SHARED, fd_, (off_t) aligned);

@@ -6,6 +6,7 @@ wire_fuzz_cpu_test: the SR4H decoders (full and shape) against damaged copies of
 compiled from the sources with AddressSanitizer and UndefinedBehaviorSanitizer.
 c_abi_cpu_test: include/strata_kv.h compiled as pedantic C99 with warnings as errors, and the entry points that
 need no GPU called from C.
+arena_fuzz_cpu_test: the hand-off arena reader against damaged arena files (headers, sizes), under the sanitizers.
 """
 import os
 import subprocess
@@ -88,3 +89,23 @@ def test_every_cxx_header_stands_alone_and_compiles_clean():
                                 "-fsyntax-only", "-I", os.path.join(ROOT, "include"), "-I", f"{CUDA}/include", tu],
                                capture_output=True, text=True, timeout=120)
             assert r.returncode == 0, n + ": " + r.stderr[-2000:]
+
+
+def test_arena_reader_refuses_damaged_arena_files_without_a_bad_access():
+    os.makedirs(BIN, exist_ok=True)
+    out = os.path.join(BIN, "arena_fuzz_cpu_test")
+    host = os.path.join(PKG, "csrc", "host")
+    srcs = [os.path.join(SRC, "arena_fuzz_cpu_test.cpp"), os.path.join(host, "handoff.cpp"),
+            os.path.join(host, "conversation_wire.cpp"), os.path.join(host, "pinned.cpp")]
+    deps = srcs + [os.path.join(ROOT, "include", "strata_kv", "handoff.hpp")]
+    if not os.path.exists(out) or any(os.path.getmtime(d) > os.path.getmtime(out) for d in deps):
+        subprocess.run(["g++", "-std=c++20", "-O1", "-g", "-fsanitize=address,undefined",
+                        "-fno-sanitize-recover=undefined", "-fno-omit-frame-pointer", "-I", os.path.join(ROOT, "include"),
+                        "-I", host, "-I", f"{CUDA}/include", "-o", out, *srcs, "-L", f"{CUDA}/lib64", "-lcudart",
+                        f"-Wl,-rpath,{CUDA}/lib64", "-pthread"], check=True)
+    with tempfile.TemporaryDirectory() as d:
+        r = subprocess.run([out, d, "2000"], capture_output=True, text=True, timeout=600,
+                           env=dict(os.environ, CUDA_VISIBLE_DEVICES="",
+                                    ASAN_OPTIONS="protect_shadow_gap=0:detect_leaks=1"))
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
+    assert ", OK" in r.stdout
