@@ -7,6 +7,7 @@ compiled from the sources with AddressSanitizer and UndefinedBehaviorSanitizer.
 c_abi_cpu_test: include/strata_kv.h compiled as pedantic C99 with warnings as errors, and the entry points that
 need no GPU called from C.
 arena_fuzz_cpu_test: the hand-off arena reader against damaged arena files (headers, sizes), under the sanitizers.
+arena_threads_cpu_test: one arena shared by four threads (claim, publish, read, release), under ThreadSanitizer.
 """
 import os
 import subprocess
@@ -109,3 +110,21 @@ def test_arena_reader_refuses_damaged_arena_files_without_a_bad_access():
                                     ASAN_OPTIONS="protect_shadow_gap=0:detect_leaks=1"))
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
     assert ", OK" in r.stdout
+
+
+def test_one_arena_shared_by_threads_has_no_data_race():
+    os.makedirs(BIN, exist_ok=True)
+    out = os.path.join(BIN, "arena_threads_cpu_test")
+    host = os.path.join(PKG, "csrc", "host")
+    srcs = [os.path.join(SRC, "arena_threads_cpu_test.cpp"), os.path.join(host, "handoff.cpp"),
+            os.path.join(host, "conversation_wire.cpp"), os.path.join(host, "pinned.cpp")]
+    deps = srcs + [os.path.join(ROOT, "include", "strata_kv", "handoff.hpp")]
+    if not os.path.exists(out) or any(os.path.getmtime(d) > os.path.getmtime(out) for d in deps):
+        subprocess.run(["g++", "-std=c++20", "-O1", "-g", "-fsanitize=thread", "-Wno-tsan", "-I",
+                        os.path.join(ROOT, "include"), "-I", host, "-I", f"{CUDA}/include", "-o", out, *srcs,
+                        "-L", f"{CUDA}/lib64", "-lcudart", f"-Wl,-rpath,{CUDA}/lib64", "-pthread"], check=True)
+    with tempfile.TemporaryDirectory() as d:
+        r = subprocess.run([out, d], capture_output=True, text=True, timeout=600,
+                           env=dict(os.environ, CUDA_VISIBLE_DEVICES="", TSAN_OPTIONS="halt_on_error=1"))
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
+    assert ", OK" in r.stdout and "WARNING: ThreadSanitizer" not in r.stderr
