@@ -68,6 +68,9 @@ def parse():
                          "time, or in port-exclusive phases (phased_schedule)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--sweep", action="store_true",
+                    help="with --impl reference: the reference's host path phase by phase (save, encode, decode, "
+                         "restore) on one pinned core at 1K / 4K / 32K / 64K / 128K tokens, one JSON line per length")
     return ap.parse_args()
 
 
@@ -426,6 +429,43 @@ def reference_pools(O, g, tokens: int):
 
 # ------------------------------------------------------------------------------------------------ arms
 
+def run_reference_sweep(O) -> None:
+    """The reference's own host hand-off path phase by phase, on one pinned core: conversation_snapshot_save,
+    conversation_wire_encode (with its FNV-1a), conversation_wire_decode, conversation_snapshot_restore.  Per
+    length a bounded sample (about 20 s of timed work, 2 to 20 repetitions; the long lengths take minutes to set
+    up), p50/p99 per phase; the split-role figure is B(T) over all four phases, the park/resume figure over save +
+    restore."""
+    g = O.Geometry()
+    try:
+        before = os.sched_getaffinity(0)
+        os.sched_setaffinity(0, {min(before)})
+    except (AttributeError, OSError):
+        before = None
+    try:
+        for t in (1024, 4096, 32768, 65536, 131072):
+            src, dst, ids = reference_pools(O, g, t)
+            save, restore = O.ref_time_park_resume(src, dst, ids, 1)   # one rep sizes the sample
+            payload, _ = O.ref_snapshot_encode(src, ids)
+            enc, dec = O.ref_time_wire(payload, 1)
+            one = float(save[0] + restore[0] + enc[0] + dec[0])
+            reps = int(max(2, min(20, 20000 // max(one, 1.0))))
+            save, restore = O.ref_time_park_resume(src, dst, ids, reps)
+            enc, dec = O.ref_time_wire(payload, reps)
+            b = O.metric_bytes(g, t)
+            pct = lambda a: {"p50": round(float(np.percentile(a, 50)), 2),  # noqa: E731
+                             "p99": round(float(np.percentile(a, 99)), 2)}
+            print(json.dumps({"impl": "reference", "sweep": True, "tokens": t, "bytes": b, "payload_bytes": len(payload),
+                              "reps": reps, "save_ms": pct(save), "encode_ms": pct(enc), "decode_ms": pct(dec),
+                              "restore_ms": pct(restore),
+                              "park_resume_gbs": round(b / (np.median(save + restore) / 1e3) / 1e9, 3),
+                              "split_role_gbs": round(b / (np.median(save + enc + dec + restore) / 1e3) / 1e9, 3),
+                              "cores": 1, "pinned": before is not None, "host": host_info()}), flush=True)
+            del src, dst, payload
+    finally:
+        if before is not None:
+            os.sched_setaffinity(0, before)
+
+
 def run_reference(args) -> None:
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -435,6 +475,9 @@ def run_reference(args) -> None:
     if not O.ref_available():
         print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libstrata_ref.so was not built "
                           "(needs the reference tree at build time)"}))
+        return
+    if args.sweep:
+        run_reference_sweep(O)
         return
     g = O.Geometry()
     try:

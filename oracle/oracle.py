@@ -340,7 +340,7 @@ def ref_snapshot_encode(pools: RefPools, ids: np.ndarray, geom_hash: int = 0, pa
     if rc:
         raise RuntimeError(f"reference refused the snapshot ({rc}): {err.value.decode()}")
     try:
-        data = C.string_at(out.value, n.value)
+        data = (C.c_char * n.value).from_address(out.value).raw   # string_at's size is 32-bit: payloads pass 2 GiB
     finally:
         ref().ref_free(out)
     return data, h.value
@@ -362,6 +362,19 @@ def ref_snapshot_bytes(pools: RefPools, ids: np.ndarray) -> int:
     if rc:
         raise RuntimeError(err.value.decode())
     return n.value
+
+
+def ref_time_wire(payload: bytes, reps: int) -> tuple:
+    """The reference's conversation_wire_encode (with its streaming FNV-1a) and conversation_wire_decode of the
+    image `payload` decodes to, timed `reps` times: (encode ms, decode ms) per rep."""
+    buf = np.frombuffer(payload, dtype=np.uint8)
+    enc = np.zeros(reps, dtype=np.float64)
+    dec = np.zeros(reps, dtype=np.float64)
+    err = C.create_string_buffer(512)
+    rc = ref().ref_time_wire(buf.ctypes.data, buf.nbytes, reps, _p(enc), _p(dec), err, 512)
+    if rc:
+        raise RuntimeError(err.value.decode())
+    return enc, dec
 
 
 def ref_time_park_resume(src: RefPools, dst: RefPools, ids: np.ndarray, reps: int) -> tuple:

@@ -181,3 +181,12 @@ def test_live_reference_transfer_failure_is_reported():
     finally:
         O.ref().ref_fail_copy_at(0)
     assert rc == 6 and "copy" in msg
+
+
+@needs_ref
+def test_live_reference_wire_timing_round_trips():
+    """The timing hook the CPU sweep uses: the reference's encode then decode (hash-checked) of a payload."""
+    s = O.make_sequence(SMALL, 100, seed=8)
+    data, _ = O.ref_snapshot_encode(O.RefPools(s), s.ids)
+    enc, dec = O.ref_time_wire(data, 3)
+    assert len(enc) == len(dec) == 3 and (enc > 0).all() and (dec > 0).all()
