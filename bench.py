@@ -436,6 +436,7 @@ def run_reference_sweep(O) -> None:
     up), p50/p99 per phase; the split-role figure is B(T) over all four phases, the park/resume figure over save +
     restore."""
     g = O.Geometry()
+    host = host_info()   # before pinning: the host's cores, not the one this run keeps
     try:
         before = os.sched_getaffinity(0)
         os.sched_setaffinity(0, {min(before)})
@@ -459,7 +460,7 @@ def run_reference_sweep(O) -> None:
                               "restore_ms": pct(restore),
                               "park_resume_gbs": round(b / (np.median(save + restore) / 1e3) / 1e9, 3),
                               "split_role_gbs": round(b / (np.median(save + enc + dec + restore) / 1e3) / 1e9, 3),
-                              "cores": 1, "pinned": before is not None, "host": host_info()}), flush=True)
+                              "cores": 1, "pinned": before is not None, "host": host}), flush=True)
             del src, dst, payload
     finally:
         if before is not None:
