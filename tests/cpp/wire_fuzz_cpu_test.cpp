@@ -127,8 +127,8 @@ int main(int argc, char** argv) {
         }
     }
     check(refused_damaged > 0, "damaged payloads are refused");
-    std::printf("wire_fuzz_cpu_test: %d damaged payloads refused, %d accepted (damage only inside blob bytes or "
-                "padding the decoders do not check), %d checks, %s\n",
+    std::printf("wire_fuzz_cpu_test: %d damaged payloads refused, %d accepted (the damage left a well-formed payload: "
+                "blob bytes, token ids, trailing bytes), %d checks, %s\n",
                 refused_damaged, accepted_damaged, checks, failures ? "FAILED" : "OK");
     return failures ? 1 : 0;
 }
