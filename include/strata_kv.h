@@ -224,6 +224,12 @@ typedef struct skv_sched_run {
 } skv_sched_run;
 SKV_API int skv_schedule_phases(const uint64_t* demand, int n_src, int n_dst, skv_sched_run* runs, int max_runs,
                                 int* n_runs, uint64_t* bound_bytes, int* n_phases);
+/* Bytes [lo, hi) of a segment list taken as one stream, as segments (a run's share of its flow).  A cut inside a
+ * segment falls on that segment's granule, rounded down: a whole page when a side is paged, 16 bytes otherwise.
+ * So adjacent ranges [a, b) and [b, c) tile the stream exactly.  Writes at most out_cap segments to `out` and their
+ * count to *n_out; SKV_ERANGE if more are needed.  Host-only. */
+SKV_API int skv_slice_segments(const skv_segment* segs, int n_segs, uint64_t lo, uint64_t hi, skv_segment* out,
+                               int out_cap, int* n_out);
 
 #ifdef __cplusplus
 }

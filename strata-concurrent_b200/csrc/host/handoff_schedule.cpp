@@ -1,5 +1,5 @@
-// handoff_schedule.cpp - skv_schedule_phases: the port-exclusive order of a many-to-many hand-off batch
-// (declared in include/strata_kv.h).  Host-only.
+// handoff_schedule.cpp - skv_schedule_phases: the port-exclusive order of a many-to-many hand-off batch, and
+// skv_slice_segments: one run's share of its flow as segments (declared in include/strata_kv.h).  Host-only.
 //
 // D[s][d] = the bytes source s hands destination d.  No order ends before the busiest port (a row or column sum,
 // M) has carried its load.  The order built here meets that bound when every port moves at one rate:
@@ -195,5 +195,41 @@ extern "C" int skv_schedule_phases(const uint64_t* demand, int n_src, int n_dst,
     for (int d = 0; d < n_dst; ++d) n_runs[d] = count[d];
     *bound_bytes = (uint64_t) M;
     *n_phases = (int) phases.size();
+    return SKV_OK;
+}
+
+extern "C" int skv_slice_segments(const skv_segment* segs, int n_segs, uint64_t lo, uint64_t hi, skv_segment* out,
+                                  int out_cap, int* n_out) {
+    using skv::fail;
+    if (n_segs < 0 || (n_segs && !segs) || out_cap < 0 || (out_cap && !out) || !n_out || hi < lo)
+        return fail(SKV_EINVAL, "skv_slice_segments: bad arguments");
+    int k = 0;
+    uint64_t at = 0;
+    for (int i = 0; i < n_segs; ++i) {
+        const skv_segment& g = segs[i];
+        const bool paged = g.src_pages || g.dst_pages;
+        const uint64_t unit = paged ? g.page_bytes : 16;
+        if (unit == 0 || g.bytes % unit)
+            return fail(SKV_EINVAL, "skv_slice_segments: segment " + std::to_string(i) +
+                                        " is not whole pages (paged) or 16-byte units (contiguous)");
+        const uint64_t s_lo = std::max(lo, at), s_hi = std::min(hi, at + g.bytes);
+        if (s_lo < s_hi) {
+            const uint64_t a = (s_lo - at) / unit * unit;
+            const uint64_t b = s_hi == at + g.bytes ? g.bytes : (s_hi - at) / unit * unit;
+            if (a < b) {
+                if (k >= out_cap) return fail(SKV_ERANGE, "skv_slice_segments: more pieces than out_cap");
+                skv_segment& o = out[k++];
+                o = g;
+                const uint64_t first_page = paged ? a / unit : 0;
+                if (!g.src_pages) o.src = static_cast<const uint8_t*>(g.src) + a;
+                if (!g.dst_pages) o.dst = static_cast<uint8_t*>(g.dst) + a;
+                if (g.src_pages) o.src_pages = g.src_pages + first_page;
+                if (g.dst_pages) o.dst_pages = g.dst_pages + first_page;
+                o.bytes = b - a;
+            }
+        }
+        at += g.bytes;
+    }
+    *n_out = k;
     return SKV_OK;
 }

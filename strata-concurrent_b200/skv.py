@@ -90,6 +90,8 @@ _SIGNATURES = {
     "skv_wait_flag": ([C.c_void_p, C.c_uint64, C.c_uint64, C.c_void_p], C.c_int),
     "skv_schedule_phases": ([C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_int, C.c_void_p, C.POINTER(C.c_uint64),
                              C.POINTER(C.c_int)], C.c_int),
+    "skv_slice_segments": ([C.c_void_p, C.c_int, C.c_uint64, C.c_uint64, C.c_void_p, C.c_int, C.POINTER(C.c_int)],
+                           C.c_int),
 }
 
 

@@ -71,3 +71,28 @@ def test_slice_segment_refuses_cuts_off_the_granule():
     for a, b in ((1, 4096), (0, 4095), (4096, 4096), (0, 4096 * 5)):
         with pytest.raises(ValueError):
             skv.slice_segment(s, a, b)
+
+
+def test_native_slicing_equals_slice_segments():
+    """skv_slice_segments (the C ABI a C++ engine uses to cut a run's share of its flow) against slice_segments."""
+    import ctypes as C
+    import numpy as np
+    segs = [skv.segment(0x10000, 0x20000, 4096 * 7, src_pages=0x100, dst_pages=0x200, page_bytes=4096,
+                        src_page_limit=50, dst_page_limit=60),
+            skv.segment(0x30000, 0x40000, 160),
+            skv.segment(0x50000, 0x60000, 4096 * 3, src_pages=0x300, page_bytes=4096, src_page_limit=9),
+            skv.segment(0x70000, 0x80000, 16, ),
+            skv.segment(0x90000, 0xA0000, 2048 * 5, dst_pages=0x400, page_bytes=2048, dst_page_limit=8)]
+    arr = (skv.Segment * len(segs))(*segs)
+    total = sum(s.bytes for s in segs)
+    key = lambda g: (g.src, g.dst, g.src_pages, g.dst_pages, g.bytes, g.page_bytes, g.src_page_limit,  # noqa: E731
+                     g.dst_page_limit)
+    rng = np.random.default_rng(9)
+    out = (skv.Segment * 16)()
+    n = C.c_int()
+    for _ in range(300):
+        lo, hi = sorted(int(x) for x in rng.integers(0, total + 1, 2))
+        skv.check(skv.lib().skv_slice_segments(arr, len(segs), lo, hi, out, 16, C.byref(n)))
+        assert [key(out[i]) for i in range(n.value)] == [key(g) for g in skv.slice_segments(segs, lo, hi)]
+    assert skv.lib().skv_slice_segments(arr, len(segs), 0, total, out, 2, C.byref(n)) == skv.ERANGE
+    assert skv.lib().skv_slice_segments(arr, len(segs), 5, 4, out, 16, C.byref(n)) == skv.EINVAL
