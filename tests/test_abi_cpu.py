@@ -93,3 +93,50 @@ def test_geometry_and_metric_bytes():
     assert g.metric_bytes(4096) == O.metric_bytes(O.Geometry(), 4096)
     off = skv.image_offsets(g, 5, 2)
     assert off[(0, 1)] == 2 * 4096 and off["total"] % 256 == 0
+
+
+def test_allocator_under_threads_never_hands_out_a_held_block():
+    """Eight threads allocate and free from one pool at once (the C calls release the GIL): a block is never
+    handed to two holders, and every block is free again at the end."""
+    import threading
+    p = fake_pool(256)
+    held, lock, errors = {}, threading.Lock(), []
+
+    def worker(t):
+        rng = np.random.default_rng(t)
+        mine = []
+        try:
+            for _ in range(400):
+                if mine and rng.random() < 0.5:
+                    k = int(rng.integers(1, len(mine) + 1))
+                    give, mine = mine[:k], mine[k:]
+                    with lock:
+                        for b in give:
+                            del held[b]
+                    p.free(give)
+                else:
+                    try:
+                        got = p.alloc(int(rng.integers(1, 9))).tolist()
+                    except skv.SkvError as e:
+                        assert e.code == skv.ENOMEM
+                        continue
+                    with lock:
+                        for b in got:
+                            assert b not in held, f"block {b} handed to thread {t} while thread {held[b]} holds it"
+                            held[b] = t
+                    mine += got
+            with lock:
+                for b in mine:
+                    del held[b]
+            p.free(mine)
+        except Exception as e:   # surfaced below: a failing thread must fail the test
+            errors.append(e)
+
+    threads = [threading.Thread(target=worker, args=(t,)) for t in range(8)]
+    for th in threads:
+        th.start()
+    for th in threads:
+        th.join()
+    assert not errors, errors[0]
+    assert p.free_count() == 256 and not held
+    p.close()
