@@ -68,6 +68,9 @@ def parse():
                          "time, or in port-exclusive phases (phased_schedule)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--timeline", action="store_true",
+                    help="config 5, phased order: add every decode GPU's per-run timeline of the last timed step "
+                         "(start and end from the step's start, bytes, source, phase, whether it waited)")
     ap.add_argument("--sweep", action="store_true",
                     help="with --impl reference: the reference's host path phase by phase (save, encode, decode, "
                          "restore) on one pinned core at 1K / 4K / 32K / 64K / 128K tokens, one JSON line per length")
@@ -1264,6 +1267,7 @@ def run_mixed(args, torch) -> dict | None:
     landed = []    # per-sequence time from the step's start (every sequence ready) to its last byte landing
     windows = []   # (handoff window, park window) per timed step, this rank
     idle = []      # phased: per timed step, the window minus this GPU's copy time
+    timeline = []  # phased, --timeline: the last timed step's runs on this GPU
     for it in range(warmup + steps):
         dist.barrier()
         torch.cuda.synchronize()
@@ -1316,6 +1320,9 @@ def run_mixed(args, torch) -> dict | None:
             landed += [h0.elapsed_time(b) for a, b in ev]
             if phased and runs:      # the share of the window this GPU spent waiting for hand-overs
                 idle.append(h0.elapsed_time(h1) - sum(a.elapsed_time(b) for a, b in rev))
+                if args.timeline:
+                    timeline = [[round(h0.elapsed_time(a), 3), round(h0.elapsed_time(b), 3), r["hi"] - r["lo"],
+                                 r["src"], r["phase"], r["wait"] is not None] for r, (a, b) in zip(runs, rev)]
     skv.set_copy_tuning(*tuning)
     status = torch.tensor([float(skv.query_status(local) != 0)], device="cuda")
     dist.all_reduce(status, op=dist.ReduceOp.MAX)
@@ -1344,7 +1351,7 @@ def run_mixed(args, torch) -> dict | None:
     # gather per-rank facts to rank 0
     facts = {"lat": lat, "landed": landed, "park_ms": [w[1] for w in windows], "hand_ms": [w[0] for w in windows],
              "bytes_in": sum(kg.metric_bytes(lengths[i]) for i in mine_in), "decode": decode,
-             "idle_ms": round(float(np.mean(idle)), 3) if idle else None,
+             "idle_ms": round(float(np.mean(idle)), 3) if idle else None, "timeline": timeline, "rank": rank,
              "launches": (sum(len(r["arrays"]) + (r["wait"] is not None) + (r["signal"] is not None) for r in runs)
                           if phased else len(pulls))}
     allf = [None] * world
@@ -1384,6 +1391,7 @@ def run_mixed(args, torch) -> dict | None:
                        "bytes_per_step": total, "serve_slots": SERVE_SLOTS, "slot_tokens": SLOT_TOKENS,
                        "order": args.mixed_order,
                        "parallelism": f"{world // 2} prefill + {world // 2} decode"},
+            **({"timeline": {f["rank"]: f["timeline"] for f in dec}} if args.timeline else {}),
             "handoffs": {"per_decode_gpu_gbs": per_decode, "idle_ms_per_decode_gpu": [f["idle_ms"] for f in dec],
                          "landed_p50_ms": round(float(np.percentile(landed_all, 50)), 4),
                          "landed_p99_ms": round(float(np.percentile(landed_all, 99)), 4),
