@@ -128,3 +128,12 @@ def test_one_arena_shared_by_threads_has_no_data_race():
                            env=dict(os.environ, CUDA_VISIBLE_DEVICES="", TSAN_OPTIONS="halt_on_error=1"))
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
     assert ", OK" in r.stdout and "WARNING: ThreadSanitizer" not in r.stderr
+
+
+def test_the_documented_integration_calls_compile():
+    """tests/cpp/integration_snippets_cpu_test.cpp holds the calls INTEGRATION.md shows, over the engine's types."""
+    r = subprocess.run(["g++", "-std=c++20", "-Wall", "-Wextra", "-Werror", "-fsyntax-only", "-I",
+                        os.path.join(ROOT, "include"), "-I", f"{CUDA}/include",
+                        os.path.join(SRC, "integration_snippets_cpu_test.cpp")], capture_output=True, text=True,
+                       timeout=120)
+    assert r.returncode == 0, r.stderr[-3000:]
