@@ -6,8 +6,9 @@
 // copies it to a second file, and in each round damages that copy - random bytes of the arena header or of a slot
 // header flipped, one 64-bit field set to an extreme value, the file cut short (also inside a slot with the header's
 // size agreeing) or lengthened - then opens it as a reader and reads every slot index (and two outside the
-// table), hashing each payload it is given.  Either step
-// may refuse; neither may fault (a payload mapped past the end of the file would raise SIGBUS and stop the run).
+// table), hashing each payload it is given, then re-opens it as a writer would after a restart and claims, publishes
+// and releases a slot of each tier.  Every step may refuse; none may fault (a payload mapped past the end of the
+// file would raise SIGBUS and stop the run).
 // Two checks pin the harness: the undamaged copy opens and its slot reads back with the writer's hash.
 //
 // Usage: arena_fuzz_cpu_test <directory> <rounds>   (exit 0 = pass)
@@ -129,7 +130,7 @@ int main(int argc, char** argv) {
     std::mt19937_64 rng(0xa7e4a5eedull);
     static const uint64_t extremes[] = {0, 1, 4096, 4095, 0xffffffffull, 0x7fffffffffffffffull, ~0ull,
                                         ~0ull - 4095, 1ull << 40, 1ull << 62};
-    int opened = 0, refused = 0;
+    int opened = 0, refused = 0, rewritten = 0;
     for (int r = 0; r < rounds; ++r) {
         restore();
         const size_t which = rng() % headers.size();
@@ -167,10 +168,28 @@ int main(int argc, char** argv) {
         }
         int s = 0;
         (read_all(s) ? opened : refused) += 1;
+        // a writer re-opening the damaged file (an instance restarting on it): refused, or it reclaims and serves
+        {
+            HandoffArena w2;
+            std::string e;
+            if (w2.open_writer(copy, sizing, kPack, kGeom, e, /*allow_existing_writer=*/true)) {
+                (void) w2.reclaim(&e);
+                (void) w2.free_slots(&e);
+                for (uint32_t tier = 0; tier < (uint32_t) sizing.tiers.size(); ++tier) {
+                    HandoffClaim c;
+                    if (w2.claim(tier, kClient, 77, c, e)) {
+                        (void) w2.write_payload(c, 0, payload.data(), 100, e);
+                        (void) w2.publish(c, 1, 100, fnv1a64(payload.data(), 100), e);
+                        (void) w2.release(c.index, c.nonce, e);
+                    }
+                }
+                ++rewritten;
+            }
+        }
     }
     check(refused > 0, "damaged arenas are refused");
     std::printf("arena_fuzz_cpu_test: %d damaged arenas refused at open, %d opened (their slots read or refused one by "
-                "one), %d checks, %s\n",
-                refused, opened, checks, failures ? "FAILED" : "OK");
+                "one), %d re-opened by a writer, %d checks, %s\n",
+                refused, opened, rewritten, checks, failures ? "FAILED" : "OK");
     return failures ? 1 : 0;
 }
