@@ -58,7 +58,7 @@ def parse():
     ap.add_argument("--p2p", default="pull", choices=["pull", "push", "push-tma"],
                     help="N > 1: the decode GPU pulls (TMA loads of peer memory), or the prefill GPU pushes (vector "
                          "engine remote stores, or TMA bulk stores to peer memory)")
-    ap.add_argument("--scenario", default="auto", choices=["auto", "pairs", "fanout", "mixed"],
+    ap.add_argument("--scenario", default="auto", choices=["auto", "pairs", "fanout", "mixed", "p2p-local"],
                     help="N > 1: pairs = N/2 prefill->decode pairs; fanout = one prefill to N-1 decodes (config 4); "
                          "mixed = N/2 prefill + N/2 decode GPUs, 64 log-uniform sequences, host parks (config 5); "
                          "auto = pairs, plus config 4 at N = 4 and config 5 at N = 8 embedded in the same line")
@@ -301,12 +301,14 @@ def relay_pieces(park_segs: list, resume_segs: list) -> list:
     return out
 
 
-def e2e_park_resume(torch, kg, src: SeqOnGpu, dst: SeqOnGpu, steps: int, warmup: int) -> dict:
+def e2e_park_resume(torch, kg, src: SeqOnGpu, dst: SeqOnGpu, steps: int, warmup: int, side_steps: int) -> dict:
     """Host-mediated handoff through the C ABI: park to pinned host, resume into another table.
 
-    staged / direct: one skv_park then one skv_resume of the whole sequence.
-    relay: the same calls chunk by chunk on two streams - skv_park of chunk c+1 (device -> host) runs while
-           skv_resume of chunk c (host -> device) runs, so both PCIe directions are busy at once."""
+    relay (the reported e2e, fixed in advance): skv_park and skv_resume chunk by chunk on two streams - the park
+           of chunk c+1 (device -> host) runs while the resume of chunk c (host -> device) runs, so both PCIe
+           directions are busy at once.  Timed over `steps` steps.
+    staged / direct (extra keys): one skv_park then one skv_resume of the whole sequence, staged through device
+           memory or with the kernel reading and writing mapped host memory.  Timed over `side_steps` steps."""
     off = skv.image_offsets(kg, src.tokens, kg.n_qsa)
     host = skv.HostBuffer(off["total"])
     staging = torch.empty(off["total"] + 256 * 64, dtype=torch.uint8, device="cuda")
@@ -323,9 +325,10 @@ def e2e_park_resume(torch, kg, src: SeqOnGpu, dst: SeqOnGpu, steps: int, warmup:
         at += (pp.bytes + 255) & ~255
     parked = [torch.cuda.Event() for _ in chunks]
     resumed = torch.cuda.Event()
-    best = None
-    parity, modes = {}, {}
-    for mode, name in ((skv.PARK_STAGED, "staged"), (skv.PARK_DIRECT, "direct"), (skv.PARK_STAGED, "relay")):
+    parity, modes, results = {}, {}, {}
+    b = kg.metric_bytes(src.tokens)
+    for mode, name, n_steps in ((skv.PARK_STAGED, "relay", steps), (skv.PARK_STAGED, "staged", side_steps),
+                                (skv.PARK_DIRECT, "direct", side_steps)):
         if name == "relay":
             def step():
                 for k, (pp, rp) in enumerate(chunks):
@@ -333,8 +336,8 @@ def e2e_park_resume(torch, kg, src: SeqOnGpu, dst: SeqOnGpu, steps: int, warmup:
                     skv.park([pp], mode, a, staging.numel() - chunk_off[k], stream)
                     parked[k].record(stream)
                     side.wait_event(parked[k])
-                    b = staging_b.data_ptr() + chunk_off[k]
-                    skv.resume([rp], mode, b, staging_b.numel() - chunk_off[k], side)
+                    b2 = staging_b.data_ptr() + chunk_off[k]
+                    skv.resume([rp], mode, b2, staging_b.numel() - chunk_off[k], side)
                 resumed.record(side)
                 stream.wait_event(resumed)
         else:
@@ -344,26 +347,22 @@ def e2e_park_resume(torch, kg, src: SeqOnGpu, dst: SeqOnGpu, steps: int, warmup:
         dst.pool_mem.zero_()
         dst.gdn.zero_()
         dst.ids.zero_()
-        total, per = time_steps(torch, stream, step, steps, warmup)
+        total, per = time_steps(torch, stream, step, n_steps, warmup)
         parity[name] = (bool(torch.equal(dst.logical(torch), src.logical(torch))) and bool(torch.equal(dst.gdn, src.gdn))
                         and bool(torch.equal(dst.ids, src.ids)))
-        b = kg.metric_bytes(src.tokens)
-        res = {"mode": name, "value": b * steps / (total / 1e3) / 1e9, "ms_per_step": total / steps,
-               "p50_ms": percentiles(per)[0], "p99_ms": percentiles(per)[1],
-               # bytes over PCIe in both directions together (B down + B up per step) per second
-               "pcie_gbs_both_directions": 2 * b * steps / (total / 1e3) / 1e9}
-        modes[name] = round(res["value"], 3)
-        if best is None or res["value"] > best["value"]:
-            best = res
-    ok = all(parity.values())
+        results[name] = {"value": b * n_steps / (total / 1e3) / 1e9, "ms_per_step": total / n_steps, "steps": n_steps,
+                         "p50_ms": percentiles(per)[0], "p99_ms": percentiles(per)[1],
+                         # bytes over PCIe in both directions together (B down + B up per step) per second
+                         "pcie_gbs_both_directions": 2 * b * n_steps / (total / 1e3) / 1e9}
+        modes[name] = round(results[name]["value"], 3)
     host.close()
-    out = {"value": round(best["value"], 3), "unit": UNIT, "h2d_bytes_per_step": kg.metric_bytes(src.tokens),
-           "d2h_bytes_per_step": kg.metric_bytes(src.tokens), "mode": best["mode"],
-           "p50_ms": round(best["p50_ms"], 3), "p99_ms": round(best["p99_ms"], 3),
-           "pcie_gbs_both_directions": round(best["pcie_gbs_both_directions"], 3),
-           "modes_gbs": modes, "api": "skv_park + skv_resume (C ABI), pinned host image",
-           "parity": ok, "parity_by_mode": parity}
-    return out
+    r = results["relay"]
+    return {"value": round(r["value"], 3), "unit": UNIT, "h2d_bytes_per_step": b, "d2h_bytes_per_step": b,
+            "mode": "relay", "steps": r["steps"], "p50_ms": round(r["p50_ms"], 3), "p99_ms": round(r["p99_ms"], 3),
+            "pcie_gbs_both_directions": round(r["pcie_gbs_both_directions"], 3),
+            "other_modes_gbs": {k: v for k, v in modes.items() if k != "relay"}, "other_modes_steps": side_steps,
+            "api": "skv_park + skv_resume (C ABI), pinned host image, 32 MB pieces on two streams",
+            "parity": parity["relay"], "parity_by_mode": parity}
 
 
 def host_info() -> dict:
@@ -470,6 +469,9 @@ def run_reference_sweep(O) -> None:
             os.sched_setaffinity(0, before)
 
 
+REFERENCE_BUDGET_S = 150.0   # wall-time cap of the reference arm's timed steps
+
+
 def run_reference(args) -> None:
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -493,20 +495,30 @@ def run_reference(args) -> None:
     threads = max(1, min(os.cpu_count() or 1, 16, int(avail * 0.6 // per_thread)))
     pools = [reference_pools(O, g, args.tokens) for _ in range(threads)]
     b = O.metric_bytes(g, args.tokens)
-    per_step = max(1, min(args.steps, 4))
+    warm = [0.0] * threads
     results = [None] * threads
 
-    def worker(i):
+    def warm_up(i):
         src, dst, ids = pools[i]
-        O.ref_time_park_resume(src, dst, ids, max(1, args.warmup // 2))   # warm-up (page faults etc.)
-        results[i] = O.ref_time_park_resume(src, dst, ids, per_step)
+        s, r = O.ref_time_park_resume(src, dst, ids, max(1, args.warmup // 2))   # page faults etc.
+        warm[i] = float(np.max(s + r)) / 1e3
 
-    ts = [threading.Thread(target=worker, args=(i,)) for i in range(threads)]
+    def worker(i, n):
+        src, dst, ids = pools[i]
+        results[i] = O.ref_time_park_resume(src, dst, ids, n)
+
+    def run_all(fn, *extra):
+        ts = [threading.Thread(target=fn, args=(i, *extra)) for i in range(threads)]
+        for t in ts:
+            t.start()
+        for t in ts:
+            t.join()
+
+    run_all(warm_up)
+    # the same step count as the device arm, unless that would take the host arm past REFERENCE_BUDGET_S
+    per_step = max(1, min(args.steps, int(REFERENCE_BUDGET_S // max(max(warm), 1e-3))))
     t0 = time.perf_counter()
-    for t in ts:
-        t.start()
-    for t in ts:
-        t.join()
+    run_all(worker, per_step)
     wall = time.perf_counter() - t0
     lat = np.concatenate([(s + r) for s, r in results])
     # aggregate: every thread moved per_step sequences; the slowest thread bounds the job
@@ -523,6 +535,9 @@ def run_reference(args) -> None:
                              "sample": f"{threads} threads x {per_step} conversation_snapshot_save+_restore each, "
                                        f"wall {wall:.1f} s", "host": host_info()},
             "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    if per_step != args.steps:
+        line["steps_note"] = (f"{args.steps} steps requested; one step of every thread took {max(warm):.2f} s in "
+                              f"warm-up, so {per_step} steps keep the host arm within {REFERENCE_BUDGET_S:.0f} s")
     print(json.dumps(line))
 
 
@@ -575,18 +590,52 @@ def run_single(args, torch) -> None:
                          "algorithmic_bytes_per_launch": 2 * b}}
     line["clocks"] = clk.summary()
     if not args.no_e2e:
-        e2e = e2e_park_resume(torch, kg, src, dst, max(3, args.steps // 4), 2)
+        e2e = e2e_park_resume(torch, kg, src, dst, args.steps, max(3, args.warmup), max(3, args.steps // 4))
         pcie = pcie_probe(torch)
         e2e["pcie_peak"] = pcie
-        # the relay keeps both directions busy, so its bound is the two-direction probe; a serial park + resume
-        # is bound by one direction at a time
-        bound = pcie["both_directions_gbs"] if e2e["mode"] == "relay" else 2 / (1 / pcie["d2h_gbs"] + 1 / pcie["h2d_gbs"])
-        e2e["pcie_frac"] = round(e2e["pcie_gbs_both_directions"] / bound, 4) if e2e["mode"] == "relay" else \
-            round(e2e["value"] * 2 / bound, 4)
+        # the relay keeps both directions busy, so its bound is the two-direction probe
+        e2e["pcie_frac"] = round(e2e["pcie_gbs_both_directions"] / pcie["both_directions_gbs"], 4)
         line["e2e"] = e2e
     if not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(t)
     print(json.dumps(line))
+
+
+def run_p2p_local(args, torch) -> None:
+    """One process, two GPUs: the decode GPU (cuda:1) pulls one sequence from the prefill GPU's pool (cuda:0) into
+    independent random slots of its own pool with the TMA engine (bulk loads of peer memory over NVLink, no
+    multicast), K steps timed with CUDA events on the decode GPU's stream.  The case a single-process profiler
+    capture of the NVLink counters runs on; the multi-process pairs (torchrun) are the headline."""
+    if torch.cuda.device_count() < 2:
+        print(json.dumps({"scenario": "p2p-local", "unavailable": "needs two GPUs"}))
+        return
+    kg = skv.KvGeometry()
+    t = args.tokens
+    n_blocks = max(args.pool_blocks, kg.n_qsa * kg.blocks(t))
+    skv.check(skv.lib().skv_enable_peer(1, 0))
+    with torch.cuda.device(0):
+        src = SeqOnGpu(torch, kg, t, n_blocks, seed=args.seed, fill=True)
+        torch.cuda.synchronize()
+    torch.cuda.set_device(1)
+    dst = SeqOnGpu(torch, kg, t, n_blocks, seed=args.seed + 1000, fill=False)
+    segs = skv.kv_segments_pool_to_pool(src.ps, dst.ps) + skv.state_segments(src.ps, dst.gdn, dst.ids)
+    arr = (skv.Segment * len(segs))(*segs)
+    stream = torch.cuda.current_stream(1)
+    L = skv.lib()
+
+    def step():
+        skv.check(L.skv_copy(arr, len(segs), skv.COPY_TMA, stream.cuda_stream))
+
+    skv.clear_status(1)
+    total, per = time_steps(torch, stream, step, args.steps, args.warmup)
+    parity = (skv.query_status(1) == 0 and bool(torch.equal(dst.logical(torch).cpu(), src.logical(torch).cpu()))
+              and bool(torch.equal(dst.gdn.cpu(), src.gdn.cpu())) and bool(torch.equal(dst.ids.cpu(), src.ids.cpu())))
+    b = kg.metric_bytes(t)
+    p50, p99 = percentiles(per)
+    print(json.dumps({"scenario": "p2p-local", "metric": METRIC, "value": round(b * args.steps / (total / 1e3) / 1e9, 3),
+                      "unit": UNIT, "tokens": t, "bytes_per_step": b, "steps": args.steps, "warmup": args.warmup,
+                      "ms_per_step": round(total / args.steps, 4), "p50_ms": round(p50, 4), "p99_ms": round(p99, 4),
+                      "parity": parity, "kernel": "copy_tma_kernel on cuda:1 loading cuda:0's pool"}))
 
 
 # ------------------------------------------------------------------------------------------------ N > 1: pairs
@@ -618,10 +667,10 @@ def summarize_pairs(max_elapsed_ms: float, per_step_ms: np.ndarray, pairs: int, 
             "p50_ms": float(np.percentile(per_step_ms, 50)), "p99_ms": float(np.percentile(per_step_ms, 99))}
 
 
-def pair_parity(torch, dist, seq, role: str, peer: int, active: bool):
+def pair_parity(torch, dist, seq, role: str, peer: int, active: bool) -> list:
     """Each side packs its copy through ITS OWN table with the gather kernel; the decode side ships its image to
-    the prefill side, which compares it with the image of the source.  A 1-element tensor, 1.0 when every pair
-    agrees (MIN over ranks)."""
+    the prefill side, which compares it with the image of the source.  One bool per pair (pair p = ranks 2p and
+    2p+1), the same list on every rank."""
     ok = torch.ones(1, device="cuda")
     if active:
         image = seq.packed(torch)
@@ -631,8 +680,63 @@ def pair_parity(torch, dist, seq, role: str, peer: int, active: bool):
             got = torch.empty_like(image)
             dist.recv(got, peer)
             ok[0] = float(bool(torch.equal(got, image)))
-    dist.all_reduce(ok, op=dist.ReduceOp.MIN)
-    return ok
+    every = [torch.zeros_like(ok) for _ in range(dist.get_world_size())]
+    dist.all_gather(every, ok)
+    return [a == 1.0 and b == 1.0 for a, b in per_pair([float(e.item()) for e in every])]
+
+
+def per_pair(values: list) -> list:
+    """One value per rank -> one (prefill's, decode's) tuple per pair: pair p is ranks 2p and 2p + 1 (an unpaired
+    last rank is left out)."""
+    return [(values[2 * p], values[2 * p + 1]) for p in range(len(values) // 2)]
+
+
+def cudart():
+    """The CUDA runtime the library itself loaded (for the copy-engine probe's cudaMemcpyAsync)."""
+    rt = ctypes.CDLL("libcudart.so.12")
+    rt.cudaMemcpyAsync.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int, ctypes.c_void_p]
+    rt.cudaMemcpyAsync.restype = ctypes.c_int
+    return rt
+
+
+PROBE_BYTES = 1 << 30
+
+
+def peer_copy_probe(torch, dist, role: str, active: bool, local_base: int, peer_base: int, nbytes: int,
+                    stream, reps: int = 5) -> dict:
+    """The NVLink reference of this run, on the same pairs: copy-engine copies (cudaMemcpyAsync between this GPU's
+    memory and the peer's CUDA-IPC mapping) of `nbytes` between the two GPUs of every pair, all pairs at once,
+    each direction in turn, median of `reps` after one untimed copy (CUDA events on the copying GPU's stream).
+    pull: the decode GPU copies the prefill GPU's pool into its own pool; push: the prefill GPU copies its pool
+    into the decode GPU's pool.  Only decode pools are written, and the hand-off overwrites them afterwards."""
+    rt = cudart()
+    world = dist.get_world_size()
+    out = {"bytes": nbytes, "reps": reps, "how": "cudaMemcpyAsync over the pair's CUDA-IPC mapping, every pair at "
+                                                 "once, median of reps, CUDA events"}
+    for direction, mover in (("pull", "decode"), ("push", "prefill")):
+        times = []
+        for _ in range(reps + 1):
+            torch.cuda.synchronize()
+            dist.barrier()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            if active and role == mover:
+                dst, src = (local_base, peer_base) if direction == "pull" else (peer_base, local_base)
+                rc = rt.cudaMemcpyAsync(dst, src, nbytes, 4, stream.cuda_stream)   # 4 = cudaMemcpyDefault
+                if rc:
+                    raise RuntimeError(f"peer copy probe: cudaMemcpyAsync returned {rc}")
+            e1.record(stream)
+            torch.cuda.synchronize()
+            times.append(e0.elapsed_time(e1))
+        mine = torch.tensor([float(np.median(times[1:])) if active and role == mover else 0.0], device="cuda")
+        every = [torch.zeros_like(mine) for _ in range(world)]
+        dist.all_gather(every, mine)
+        who = 1 if mover == "decode" else 0
+        gbs = [round(nbytes / (pair[who] / 1e3) / 1e9, 1) for pair in per_pair([float(e.item()) for e in every])]
+        out[f"{direction}_gbs"] = gbs
+        out[f"{direction}_gbs_median"] = round(float(np.median(gbs)), 1)
+    dist.barrier()
+    return out
 
 
 def host_relay_pairs(args, torch, dist, kg, t: int, seq, role: str, peer: int, active: bool, stream,
@@ -717,24 +821,29 @@ def host_relay_pairs(args, torch, dist, kg, t: int, seq, role: str, peer: int, a
     value = pairs * b * steps / (float(el[0].item()) / 1e3) / 1e9
     return {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": pairs * b, "d2h_bytes_per_step": pairs * b,
             "ms_per_step": round(float(el[0].item()) / steps, 4), "per_pair_gbs": round(value / pairs, 3),
-            "parity": bool(ok.item() == 1.0) and el[1].item() == 0, "steps": steps,
+            "parity": all(ok) and el[1].item() == 0, "parity_by_pair": ok, "steps": steps,
             "api": "skv_park on the prefill GPU into pinned memory shared with its decode rank (memfd + "
                    "skv_host_register), skv_resume on the decode GPU, per-piece flags in that host memory",
             "note": "the reference's multi-GPU route (through pinned RAM), PCIe-bound per pair"}
 
 
-def run_pairs(args, torch) -> dict | None:
+def run_pairs(args, torch, tokens: int | None = None, steps: int | None = None, e2e: bool = True,
+              probe: dict | None = None) -> tuple:
     """N/2 prefill->decode pairs.  pull (default): the decode GPU's copy kernel reads the prefill GPU's pool
     pages over NVLink (TMA bulk loads from peer memory, no multicast) and writes its own pool; push: the
     prefill GPU's vector kernel stores into the decode GPU's pool.  Either way the destination slots are written
     directly, with no intermediate contiguous copy.  Protocol per step (flags are 8-byte words, release
     stores / bounded acquire polls): pull = prefill raises READY on the decode GPU, decode waits READY, pulls,
     raises DONE on the prefill GPU (whose blocks may then be freed), prefill waits DONE; push = prefill pushes
-    and raises ARRIVED, decode waits ARRIVED."""
+    and raises ARRIVED, decode waits ARRIVED.
+
+    `probe`: the peer-copy reference of this run; measured here (before the hand-offs) when None.  Returns
+    (rank 0's line or None, the probe)."""
     import torch.distributed as dist
     rank, world, local = ranks()
     kg = skv.KvGeometry()
-    t = args.tokens
+    t = tokens or args.tokens
+    n_steps = steps or args.steps
     pairs = world // 2
     role, peer, active = pair_role(rank, world)
     lay = state_layout(kg, t)
@@ -756,6 +865,7 @@ def run_pairs(args, torch) -> dict | None:
     dist.all_gather_object(handles, mine)
     imported = []
     step = None
+    peer_pool = 0
     if active:
         other = handles[peer]
         peer_pool = skv.ipc_import(local, other["pool"])
@@ -796,31 +906,37 @@ def run_pairs(args, torch) -> dict | None:
     if step is None:
         def step():
             pass
+    if probe is None:
+        probe = peer_copy_probe(torch, dist, role, active, seq.pool.base if active else 0, peer_pool,
+                                min(PROBE_BYTES, n_blocks * kg.block_bytes), stream)
     skv.clear_status(local)
     dist.barrier()
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
     dist.barrier()
-    ev = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(n_steps + 1)]
     with Clocks(local) as clk:
         ev[0].record(stream)
-        for i in range(args.steps):
+        for i in range(n_steps):
             step()
             ev[i + 1].record(stream)
         torch.cuda.synchronize()
     dist.barrier()
-    per = torch.tensor([ev[i].elapsed_time(ev[i + 1]) for i in range(args.steps)], device="cuda")
+    per = torch.tensor([ev[i].elapsed_time(ev[i + 1]) for i in range(n_steps)], device="cuda")
     status = skv.query_status(local)
-    red = torch.tensor([ev[0].elapsed_time(ev[args.steps]), float(status != 0)], device="cuda")
+    red = torch.tensor([ev[0].elapsed_time(ev[n_steps]), float(status != 0)], device="cuda")
     dist.all_reduce(red, op=dist.ReduceOp.MAX)
     dist.all_reduce(per, op=dist.ReduceOp.MAX)
     ok = pair_parity(torch, dist, seq, role, peer, active)
-    e2e = None if args.no_e2e else host_relay_pairs(args, torch, dist, kg, t, seq, role, peer, active, stream, pairs)
-    res = summarize_pairs(float(red[0].item()), per.cpu().numpy(), pairs, kg.metric_bytes(t), args.steps)
+    relay = None
+    if e2e and not args.no_e2e:
+        relay = host_relay_pairs(args, torch, dist, kg, t, seq, role, peer, active, stream, pairs)
+    res = summarize_pairs(float(red[0].item()), per.cpu().numpy(), pairs, kg.metric_bytes(t), n_steps)
     line = None
     if rank == 0:
-        line = {"metric": METRIC, "value": round(res["value"], 3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        ref = probe["pull_gbs_median"] if pull else probe["push_gbs_median"]
+        line = {"metric": METRIC, "value": round(res["value"], 3), "unit": UNIT, "n_gpus": world, "steps": n_steps,
                 "warmup": args.warmup, "ms_per_step": round(res["ms_per_step"], 4), "p50_ms": round(res["p50_ms"], 4),
                 "p99_ms": round(res["p99_ms"], 4), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
                 "dtype": "u8", "data": "synthetic",
@@ -829,21 +945,101 @@ def run_pairs(args, torch) -> dict | None:
                                        f"into independent random slots of the decode GPU's {n_blocks}-block pool",
                            "tokens": t, "pairs": pairs, "p2p": args.p2p, "bytes_per_step_per_pair": kg.metric_bytes(t),
                            "l2": "inputs larger than L2", "parallelism": f"{pairs} prefill/decode pairs"},
-                "parity": bool(ok.item() == 1.0) and red[1].item() == 0, "gpu_launches": args.steps * (4 if pull else 3) * pairs,
-                "roofline": {"bound": "nvlink", "achieved": round(res["per_pair_gbs"], 1), "peak": NVLINK_PEER_COPY_GBS,
-                             "unit": "GB/s", "frac": round(res["per_pair_gbs"] / NVLINK_PEER_COPY_GBS, 4),
+                "parity": all(ok) and red[1].item() == 0, "parity_by_pair": ok,
+                "gpu_launches": n_steps * (4 if pull else 3) * pairs,
+                "roofline": {"bound": "nvlink", "achieved": round(res["per_pair_gbs"], 1), "peak": ref,
+                             "unit": "GB/s", "frac": round(res["per_pair_gbs"] / ref, 4),
                              "frac_of_nominal_900": round(res["per_pair_gbs"] / 900.0, 4),
-                             "peak_kind": "measured peer copy per direction (profiling recipe); 900 nominal",
+                             "peak_kind": f"peer copy of this run ({'pull' if pull else 'push'} direction, "
+                                          "peer_copy_probe); 900 GB/s per direction nominal",
                              "traffic": None, "kernel": "copy_vec_kernel" if args.p2p == "push" else "copy_tma_kernel"},
+                "peer_copy_probe": probe,
                 "clocks": clk.summary()}
-        if e2e is not None:
-            line["e2e"] = e2e
+        if relay is not None:
+            line["e2e"] = relay
     torch.cuda.synchronize()
     dist.barrier()
     for p in imported:
         skv.ipc_close(p)
     dist.barrier()
-    return line if rank == 0 else None
+    return (line if rank == 0 else None), probe
+
+
+SWEEP_TOKENS = (1024, 4096, 32768, 131072)   # config 3's lengths
+
+
+def pair_sweep(args, torch, probe: dict, headline: dict | None) -> list | None:
+    """Config 3's length sweep on the same pairs and probe: every length of SWEEP_TOKENS but the headline's own
+    (reused), each a short run of its own with parity."""
+    rows = []
+    for t in SWEEP_TOKENS:
+        if t == args.tokens:
+            sub = headline
+        else:
+            sub, _ = run_pairs(args, torch, tokens=t, steps=min(args.steps, 50), e2e=False, probe=probe)
+        if sub is not None:
+            rows.append({"tokens": t, "bytes": sub["config"]["bytes_per_step_per_pair"], "steps": sub["steps"],
+                         "value": sub["value"], "ms_per_step": sub["ms_per_step"], "p50_ms": sub["p50_ms"],
+                         "p99_ms": sub["p99_ms"], "per_pair_gbs": sub["roofline"]["achieved"],
+                         "frac_of_probe": sub["roofline"]["frac"],
+                         "frac_of_nominal_900": sub["roofline"]["frac_of_nominal_900"], "parity": sub["parity"]})
+    return rows if headline is not None else None
+
+
+SPLIT_ROLE_TOKENS = (4096, 32768)
+
+
+def split_roles(torch, rank: int) -> list | None:
+    """Row f2 on this run's GPUs 0 and 1: the split-role hand-off across two processes with only a device
+    descriptor in the hand-off slot (tests/cpp/handoff_device_gpu_test.cpp: prefill process on GPU 0 packs the
+    whole session into its HBM and publishes the descriptor; decode process on GPU 1 reads the slot, mounts
+    straight from GPU 0's HBM and checks every byte), at config 1's length and at 32K.  Rank 0 runs it while every
+    rank holds no work on its GPU: the other ranks wait on the rendezvous store (a host wait), not in a
+    collective.  Returns rank 0's records."""
+    import re
+    import subprocess
+    import tempfile
+    from datetime import timedelta
+
+    import torch.distributed as dist
+    store = dist.distributed_c10d._get_default_store()
+    torch.cuda.synchronize()
+    dist.barrier()
+    torch.cuda.synchronize()
+    key = "skv_split_roles_done"
+    rows = None
+    if rank == 0:
+        rows = []
+        try:
+            sys.path.insert(0, os.path.join(ROOT, "tests"))
+            from test_cpp_gpu import build as build_cpp_test
+            exe = build_cpp_test("handoff_device_gpu_test")
+            for t in SPLIT_ROLE_TOKENS:
+                with tempfile.TemporaryDirectory() as d:
+                    r = subprocess.run([exe, d, str(t)], capture_output=True, text=True, timeout=400)
+                out = r.stdout
+                pub = re.search(r"publish \(pack into HBM \+ descriptor\) ([0-9.]+) ms; fastest claim-to-release "
+                                r"\(publish, DONE, decode mount, ACK, release\) ([0-9.]+) ms for ([0-9]+) payload bytes", out)
+                mnt = re.search(r"read the slot \+ mount from the peer's HBM ([0-9.]+) ms", out)
+                checks = [int(c) for c in re.findall(r"([0-9]+) checks passed", out)]
+                row = {"tokens": t, "rc": r.returncode, "parity": r.returncode == 0 and "both instances passed" in out,
+                       "checks": sum(checks)}
+                if pub and mnt:
+                    nbytes = int(pub.group(3))
+                    row.update({"payload_bytes": nbytes, "publish_ms": float(pub.group(1)),
+                                "mount_ms": float(mnt.group(1)), "claim_to_release_ms": float(pub.group(2)),
+                                "mount_gbs_over_nvlink": round(nbytes / (float(mnt.group(1)) / 1e3) / 1e9, 1)})
+                if r.returncode:
+                    row["tail"] = (out + r.stderr)[-400:]
+                rows.append(row)
+        except Exception as e:   # the record says why; the headline stands
+            rows.append({"error": f"{type(e).__name__}: {e}"[:400]})
+        finally:
+            store.set(key, "1")
+    else:
+        store.wait([key], timedelta(seconds=1200))
+    dist.barrier()
+    return rows
 
 
 # ------------------------------------------------------------------------------------------------ fan-out
@@ -1058,14 +1254,14 @@ def run_fanout(args, torch, tokens: int | None = None, steps: int | None = None)
                              "p50_ms": round(float(np.percentile(per, 50)), 4),
                              "p99_ms": round(float(np.percentile(per, 99)), 4),
                              "per_receiver_gbs": round(b * n_steps / (tot / 1e3) / 1e9, 3), "parity": ok}
-        best = max(methods, key=lambda k: methods[k]["value"])
+        best = "chain_push"   # the reported method, fixed in advance; the others are kept beside it in `methods`
         m = methods[best]
         line = {"metric": METRIC, "value": m["value"], "unit": UNIT, "n_gpus": world, "steps": n_steps,
                 "warmup": args.warmup, "ms_per_step": m["ms_per_step"], "p50_ms": m["p50_ms"], "p99_ms": m["p99_ms"],
                 "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u8", "data": "synthetic",
                 "config": {"workload": f"config 4: 1 prefill GPU fans one {t}-token cache out to {receivers} decode "
-                                       f"GPUs (independent random tables); best of p2p / nccl broadcast / chained pull / "
-                                       f"chained push",
+                                       f"GPUs (independent random tables); reported: the chained push (p2p, nccl "
+                                       f"broadcast and chained pull timed beside it)",
                            "tokens": t, "receivers": receivers, "method": best, "chunk_mb": args.chunk_mb,
                            "l2": "inputs larger than L2", "parallelism": f"1 -> {receivers} fan-out"},
                 "methods": methods, "parity": all(v["parity"] for v in methods.values()) and status.item() == 0,
@@ -1447,6 +1643,9 @@ def main() -> None:
         return
     import torch
     world = int(os.environ.get("WORLD_SIZE", "1"))
+    if world == 1 and args.scenario == "p2p-local":
+        run_p2p_local(args, torch)
+        return
     if world == 1:
         run_single(args, torch)
         return
@@ -1463,7 +1662,13 @@ def main() -> None:
         else:
             # the headline: N/2 pairs (configs 3/5 throughput, weak scaling); at N = 4 and N = 8 the same run also
             # measures BASELINE's own 4- and 8-GPU configs and embeds them
-            line = run_pairs(args, torch)
+            line, probe = run_pairs(args, torch)
+            if args.scenario == "auto" and world == 2:
+                sweep = pair_sweep(args, torch, probe, line)
+                roles = split_roles(torch, rank)
+                if line is not None:
+                    line["config3_sweep"] = sweep
+                    line["split_roles_device_descriptor"] = roles
             if args.scenario == "auto" and world == 4:
                 sub = run_fanout(args, torch, tokens=65536, steps=min(args.steps, 40))
                 if line is not None:

@@ -33,12 +33,14 @@ class Placed:
     """A Sequence placed into a pool: host mirror of the whole pool + device copy + the PooledSequence."""
 
     def __init__(self, torch, g: O.Geometry, seq: O.Sequence, n_blocks: int, seed: int, layers: int,
-                 canary: int = 0, upload: bool = True):
+                 canary: int = 0, upload: bool = True, device: int = 0):
         self.torch = torch
+        self.device = device
+        where = f"cuda:{device}"
         self.kg = kg = kvg(g)
         self.host_pool = np.full(n_blocks * kg.block_bytes, canary, dtype=np.uint8)
-        self.dev_pool = torch.empty(n_blocks * kg.block_bytes, dtype=torch.uint8, device="cuda")
-        self.pool = skv.Pool(0, n_blocks, kg.block_bytes, memory=self.dev_pool)
+        self.dev_pool = torch.empty(n_blocks * kg.block_bytes, dtype=torch.uint8, device=where)
+        self.pool = skv.Pool(device, n_blocks, kg.block_bytes, memory=self.dev_pool)
         self.pool.scramble(seed)
         nb = kg.blocks(seq.tokens)
         self.blocks = np.stack([self.pool.alloc(nb) for _ in range(layers)]) if layers else np.zeros((0, nb), np.int32)
@@ -52,14 +54,25 @@ class Placed:
                 O.scatter_pages(seq.k[layer], k_table, pages, kg.page_bytes, self.host_pool)
                 O.scatter_pages(seq.v[layer], v_table, pages, kg.page_bytes, self.host_pool)
         self.dev_pool.copy_(torch.from_numpy(self.host_pool))
-        self.dev_tables = torch.from_numpy(tables.reshape(-1).copy()).cuda()
+        self.dev_tables = torch.from_numpy(tables.reshape(-1).copy()).to(where)
         ids_pad = np.zeros(((4 * seq.tokens + 15) // 16) * 4, dtype=np.int32)
         ids_pad[:seq.tokens] = seq.ids if upload else 0
-        self.dev_gdn = torch.from_numpy(seq.gdn.copy() if upload else np.zeros_like(seq.gdn)).cuda()
-        self.dev_ids = torch.from_numpy(ids_pad).cuda()
+        self.dev_gdn = torch.from_numpy(seq.gdn.copy() if upload else np.zeros_like(seq.gdn)).to(where)
+        self.dev_ids = torch.from_numpy(ids_pad).to(where)
         self.ps = skv.PooledSequence(kg, self.pool, seq.tokens, layers, self.blocks, self.dev_tables, self.dev_gdn,
                                      self.dev_ids)
-        torch.cuda.synchronize()
+        torch.cuda.synchronize(device)
+
+    def expected_pool(self, seq: O.Sequence) -> np.ndarray:
+        """This pool as the oracle writes it: the host mirror with every layer of `seq` scattered through THIS
+        placement's block tables (slots the sequence does not own keep their canary)."""
+        kg = self.kg
+        expect = self.host_pool.copy()
+        for j in range(len(self.blocks)):
+            kt, vt = skv.layer_page_tables(kg, self.blocks[j])
+            O.scatter_pages(seq.k[j], kt, kg.pages(seq.tokens), kg.page_bytes, expect)
+            O.scatter_pages(seq.v[j], vt, kg.pages(seq.tokens), kg.page_bytes, expect)
+        return expect
 
 
 def run(torch, segs, engine):

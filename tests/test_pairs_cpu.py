@@ -174,7 +174,12 @@ def _rank(rank, world, port, q):
         dist.all_reduce(elapsed, op=dist.ReduceOp.MAX)
         dist.all_reduce(per, op=dist.ReduceOp.MAX)
         res = bench.summarize_pairs(float(elapsed[0]), per.numpy(), world // 2, 1000, 3)
-        q.put((rank, checks, float(elapsed[0]), per.tolist(), res["value"]))
+        # the per-pair verdicts and probe times as the bench gathers them: every rank's value, split by pair
+        mine_t = torch.tensor([float(rank == 1)])
+        every = [torch.zeros_like(mine_t) for _ in range(world)]
+        dist.all_gather(every, mine_t)
+        pairs = bench.per_pair([float(e.item()) for e in every])
+        q.put((rank, checks, float(elapsed[0]), per.tolist(), res["value"], pairs))
     finally:
         dist.destroy_process_group()
 
@@ -188,8 +193,8 @@ def test_two_rank_exchange_and_reductions():
         p.start()
     out = {}
     for _ in procs:
-        rank, checks, elapsed, per, value = q.get(timeout=120)
-        out[rank] = (checks, elapsed, per, value)
+        rank, checks, elapsed, per, value, pairs = q.get(timeout=120)
+        out[rank] = (checks, elapsed, per, value, pairs)
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0
@@ -197,6 +202,12 @@ def test_two_rank_exchange_and_reductions():
     assert out[0][1] == out[1][1] == 11.0
     assert out[0][2] == [2.0, 2.0, 3.0]
     assert out[0][3] == pytest.approx(1 * 1000 * 3 / 0.011 / 1e9)
+    assert out[0][4] == out[1][4] == [(0.0, 1.0)]
+
+
+def test_per_pair_split():
+    assert bench.per_pair([1, 2, 3, 4, 5, 6, 7, 8]) == [(1, 2), (3, 4), (5, 6), (7, 8)]
+    assert bench.per_pair([1, 2, 3]) == [(1, 2)]        # an unpaired last rank idles
 
 
 def _fake_sequence_segments(kg, i, tokens):
