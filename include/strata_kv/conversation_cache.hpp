@@ -1,6 +1,7 @@
 // include/strata_kv/conversation_cache.hpp - parked conversations: the image types and the park store.
 //
-// Interface and policy of the reference's include/strata/core/conversation_cache.hpp:47-456, implemented here:
+// Interface and policy of the reference's include/strata/core/conversation_cache.hpp:47-456, written here from the
+// policy (the class comment below states it):
 //   * the image types (ConversationCheckpoint, ConversationKv, ConversationKvReuse, ConversationStageSnapshot,
 //     SavedConversation) with their byte accounting.  The K/V streams (over 90 % of a park's bytes) are pinned
 //     ConversationBuffers; the running-state vectors keep the reference's plain std::vector<uint8_t> type so
@@ -19,7 +20,7 @@
 #include <array>
 #include <cstddef>
 #include <cstdint>
-#include <deque>
+#include <optional>
 #include <utility>
 #include <vector>
 
@@ -135,6 +136,18 @@ int64_t conversation_same_branch(const ConversationCheckpoint& c, const std::vec
     return conversation_match_detail::images_agree(c, images, n) ? (int64_t) n : 0;
 }
 
+/// The park store.  Its policy, as the engine relies on it:
+///   * capacity: at most `slots` entries, and the entries plus the retained K/V within `budget` bytes (an image's
+///     bytes() at the time it was parked);
+///   * use clock: every park, every match handed out (best, best_exact) and every touch() stamps the entry with the
+///     next tick; a take() advances the clock too, so a later park is newer than everything before it;
+///   * eviction: entries no request has claimed go first, least recently used first; only when every entry is
+///     claimed does the least recently used claimed one go.  The retained K/V is dropped before any entry;
+///   * claims: an entry parked with an owner is offered to that request (and to callers that name no request),
+///     never to another request, until release_owner();
+///   * matching: the longest strict prefix of a prompt over every entry's live branch and retained checkpoints
+///     (best / probe), or the live branch that IS a given branch (best_exact); among equal lengths the newest
+///     entry wins, and within an entry its live branch before its checkpoints.
 class ConversationCache {
 public:
     struct Match {
@@ -147,161 +160,162 @@ public:
     ConversationCache(size_t budget, size_t slots) : budget_(budget), slots_(slots) {}
 
     bool enabled() const { return budget_ != 0 && slots_ != 0; }
-    size_t bytes() const { return parked_bytes_ + retained_.bytes(); }
-    size_t size() const { return entries_.size(); }
+    size_t bytes() const { return parked_ + kept_.bytes(); }
+    size_t size() const { return shelf_.size(); }
     size_t slots() const { return slots_; }
     size_t budget() const { return budget_; }
     size_t evictions() const { return evictions_; }
     uint64_t clock() const { return clock_; }
-    uint64_t use(size_t index) const { return stamps_.at(index); }
+    uint64_t use(size_t index) const { return shelf_.at(index).last_use; }
 
-    /// Keep the K/V a mount just restored, for an incremental re-park; never evicts anything to fit.
+    /// Keep the K/V a mount just restored (all of it valid for `tokens` tokens) for an incremental re-park, if it
+    /// fits beside the parked entries; nothing is evicted for it.
     void retain(std::vector<ConversationKv>&& kv, int64_t tokens) {
-        retained_ = {};
-        ConversationKvReuse candidate{std::move(kv), tokens, tokens};
-        if (enabled() && candidate.bytes() <= budget_ - parked_bytes_) retained_ = std::move(candidate);
+        kept_ = {};
+        ConversationKvReuse offer{std::move(kv), tokens, tokens};
+        if (enabled() && offer.bytes() <= budget_ - parked_) kept_ = std::move(offer);
     }
-    /// A rewrite at `first_dirty` bounds how much of the retained K/V is still valid.
+    /// The session was rewritten from token `first_dirty` on: the retained K/V is valid only before it.
     void limit_reuse(int64_t first_dirty) {
-        retained_.unchanged_tokens = std::min(retained_.unchanged_tokens, first_dirty);
-        if (retained_.unchanged_tokens <= 0) retained_ = {};
+        kept_.unchanged_tokens = std::min(kept_.unchanged_tokens, first_dirty);
+        if (kept_.unchanged_tokens <= 0) kept_ = {};
     }
-    ConversationKvReuse take_reuse() { return std::exchange(retained_, {}); }
-    size_t retained_bytes() const { return retained_.bytes(); }
+    ConversationKvReuse take_reuse() { return std::exchange(kept_, {}); }
+    size_t retained_bytes() const { return kept_.bytes(); }
 
+    /// `incoming` bytes could be parked beside `held` bytes (an image taken out and still alive) without evicting.
     bool can_fit(size_t incoming, size_t held = 0) const {
-        if (!enabled() || held > budget_ || incoming > budget_ - held) return false;
-        return entries_.size() < slots_ && bytes() <= budget_ - held - incoming;
+        const std::optional<size_t> room = headroom(incoming, held);
+        return room && shelf_.size() < slots_ && bytes() <= *room;
     }
 
-    /// Index of the smallest stamp; equal stamps resolve to the earlier index.  0 for n == 0.
+    /// The position of the smallest stamp among `n`, the earlier position on a tie; 0 when n is 0.
     static size_t lru_victim(const uint64_t* stamps, size_t n) {
-        size_t best = 0;
-        for (size_t i = 1; i < n; ++i)
-            if (stamps[i] < stamps[best]) best = i;
-        return best;
+        return (size_t) (std::min_element(stamps, stamps + n) - stamps);
     }
 
-    /// The longest reusable prefix for `prompt`, among entries not claimed by another request (a hit is a use).
+    /// The longest reusable prefix of `prompt` among the entries offered to `requester`; a hit counts as a use.
     template <class Token>
     Match best(const std::vector<Token>& prompt, const std::vector<ConversationImageKey>& images, bool cvec,
                int64_t requester = kNoOwner) {
-        const Match m = search(prompt, images, cvec, requester);
+        const Match m = longest_prefix(prompt, images, cvec, requester);
         if (m.tokens > 0) touch(m.index);
         return m;
     }
 
-    /// The same search without counting it as a use.
+    /// best() without counting the hit as a use.
     template <class Token>
     Match probe(const std::vector<Token>& prompt, const std::vector<ConversationImageKey>& images, bool cvec,
                 int64_t requester = kNoOwner) const {
-        return search(prompt, images, cvec, requester);
+        return longest_prefix(prompt, images, cvec, requester);
     }
 
-    /// The parked LIVE branch that is exactly `branch` (a hand-over back to the slot that parked it).
+    /// The parked live branch that is exactly `branch` (a hand-back to the slot that parked it); a hit is a use.
     template <class Token>
     Match best_exact(const std::vector<Token>& branch, const std::vector<ConversationImageKey>& images, bool cvec,
                      int64_t requester = kNoOwner) {
-        Match found;
-        for (size_t i = entries_.size(); i-- > 0;) {
-            const SavedConversation& e = entries_[i];
-            if (e.cvec != cvec || claimed_by_other(i, requester)) continue;
-            const int64_t n = conversation_same_branch(e.live, branch, images);
-            if (n > found.tokens) found = Match{i, n, true};
-        }
-        if (found.tokens > 0) touch(found.index);
-        return found;
+        Match m;
+        for_each_offered(cvec, requester, [&](size_t i, const SavedConversation& e) {
+            keep_longer(m, i, conversation_same_branch(e.live, branch, images), true);
+        });
+        if (m.tokens > 0) touch(m.index);
+        return m;
     }
 
-    void touch(size_t index) { stamps_.at(index) = ++clock_; }
+    void touch(size_t index) { shelf_.at(index).last_use = ++clock_; }
 
+    /// Entry `index` belongs to a request other than `requester` (requests that name none see every entry).
     bool claimed_by_other(size_t index, int64_t requester) const {
-        const int64_t o = entries_.at(index).owner;
-        return o != kNoOwner && requester != kNoOwner && o != requester;
+        const int64_t holder = shelf_.at(index).image.owner;
+        return holder != kNoOwner && requester != kNoOwner && holder != requester;
     }
     void release_owner(int64_t id) {
-        for (auto& e : entries_)
-            if (e.owner == id) e.owner = kNoOwner;
+        for (Parked& p : shelf_)
+            if (p.image.owner == id) p.image.owner = kNoOwner;
     }
-    int64_t owner(size_t index) const { return entries_.at(index).owner; }
+    int64_t owner(size_t index) const { return shelf_.at(index).image.owner; }
 
-    /// Remove and return the entry (a mount).  The clock advances so the next park is newer than all entries.
+    /// Hand entry `index` out for a mount; the clock moves on so that the next park is the newest entry.
     SavedConversation take(size_t index) {
-        SavedConversation out = std::move(entries_.at(index));
-        parked_bytes_ -= out.bytes();
-        drop(index);
+        Parked p = std::move(shelf_.at(index));
+        shelf_.erase(shelf_.begin() + (std::ptrdiff_t) index);
+        parked_ -= p.bytes;
         ++clock_;
-        return out;
+        return std::move(p.image);
     }
 
-    /// Evict until `incoming` bytes fit beside `held` (an image taken out but still alive) and a slot is free.
+    /// Evict (the retained K/V first, then entries in eviction order) until `incoming` bytes fit beside `held` and a
+    /// slot is free.  False, with nothing evicted, when `incoming` and `held` alone exceed the budget.
     bool make_room(size_t incoming, size_t held = 0) {
-        if (!enabled() || held > budget_ || incoming > budget_ - held) return false;
-        const size_t room = budget_ - held - incoming;
-        if (bytes() > room) retained_ = {};
-        while (!entries_.empty() && (entries_.size() >= slots_ || parked_bytes_ > room)) {
+        const std::optional<size_t> room = headroom(incoming, held);
+        if (!room) return false;
+        if (bytes() > *room) kept_ = {};
+        while (!shelf_.empty() && (shelf_.size() >= slots_ || parked_ > *room)) {
             const size_t v = victim_to_prune();
-            parked_bytes_ -= entries_[v].bytes();
-            drop(v);
+            parked_ -= shelf_[v].bytes;
+            shelf_.erase(shelf_.begin() + (std::ptrdiff_t) v);
             ++evictions_;
         }
         return true;
     }
 
-    /// Least recently used among unclaimed entries; least recently used overall when all are claimed.
+    /// The entry eviction takes next: unclaimed before claimed, then the least recently used, then the oldest park.
     size_t victim_to_prune() const {
-        if (entries_.empty()) return 0;
-        bool have_free = false;
-        size_t best = 0;
-        for (size_t i = 0; i < entries_.size(); ++i) {
-            if (entries_[i].owner != kNoOwner) continue;
-            if (!have_free || stamps_[i] < stamps_[best]) best = i;
-            have_free = true;
-        }
-        return have_free ? best : lru_victim(stamps_.data(), stamps_.size());
+        const auto order = [](const Parked& p) { return std::make_pair(p.image.owner != kNoOwner, p.last_use); };
+        const auto it = std::min_element(shelf_.begin(), shelf_.end(),
+                                          [&](const Parked& a, const Parked& b) { return order(a) < order(b); });
+        return (size_t) (it - shelf_.begin());
     }
 
-    /// Park `image`, claimed by `owner` (kNoOwner: the cache's).  False when it cannot fit at all.
+    /// Park `image` for `owner` (kNoOwner: anyone may take it), evicting as needed.  False when it cannot fit.
     bool put(SavedConversation&& image, int64_t owner = kNoOwner, size_t held = 0) {
         const size_t n = image.bytes();
         if (!make_room(n, held)) return false;
         image.owner = owner;
-        entries_.push_back(std::move(image));
-        stamps_.push_back(++clock_);
-        parked_bytes_ += n;
+        shelf_.push_back(Parked{std::move(image), n, ++clock_});
+        parked_ += n;
         return true;
     }
 
 private:
-    void drop(size_t index) {
-        entries_.erase(entries_.begin() + (std::ptrdiff_t) index);
-        stamps_.erase(stamps_.begin() + (std::ptrdiff_t) index);
+    struct Parked {
+        SavedConversation image;
+        size_t bytes = 0;        ///< image.bytes() when it was parked
+        uint64_t last_use = 0;   ///< the clock tick of its park or its latest use
+    };
+
+    /// Budget left once `held` and `incoming` are set aside, or nothing when the cache is off or they exceed it.
+    std::optional<size_t> headroom(size_t incoming, size_t held) const {
+        if (!enabled() || held > budget_ || incoming > budget_ - held) return std::nullopt;
+        return budget_ - held - incoming;
     }
 
-    /// Longest exact prefix over every entry's live branch and checkpoints, newest entry first; equal lengths
-    /// keep the first found (the newest entry, its live branch before its checkpoints).
+    /// fn(index, image) for every entry offered to `requester` under conditioning `cvec`, newest park first.
+    template <class Fn>
+    void for_each_offered(bool cvec, int64_t requester, Fn&& fn) const {
+        for (size_t i = shelf_.size(); i-- > 0;)
+            if (shelf_[i].image.cvec == cvec && !claimed_by_other(i, requester)) fn(i, shelf_[i].image);
+    }
+    /// A candidate replaces the match only when it is strictly longer, so the first of equal lengths stays.
+    static void keep_longer(Match& m, size_t index, int64_t tokens, bool live) {
+        if (tokens > m.tokens) m = Match{index, tokens, live};
+    }
+
     template <class Token>
-    Match search(const std::vector<Token>& prompt, const std::vector<ConversationImageKey>& images, bool cvec,
-                 int64_t requester) const {
-        Match found;
-        for (size_t i = entries_.size(); i-- > 0;) {
-            const SavedConversation& e = entries_[i];
-            if (e.cvec != cvec || claimed_by_other(i, requester)) continue;
-            const int64_t live = conversation_prefix(e.live, prompt, images);
-            if (live > found.tokens) found = Match{i, live, true};
-            for (const auto& c : e.checkpoints) {
-                const int64_t n = conversation_prefix(c, prompt, images);
-                if (n > found.tokens) found = Match{i, n, false};
-            }
-        }
-        return found;
+    Match longest_prefix(const std::vector<Token>& prompt, const std::vector<ConversationImageKey>& images, bool cvec,
+                         int64_t requester) const {
+        Match m;
+        for_each_offered(cvec, requester, [&](size_t i, const SavedConversation& e) {
+            keep_longer(m, i, conversation_prefix(e.live, prompt, images), true);
+            for (const ConversationCheckpoint& c : e.checkpoints) keep_longer(m, i, conversation_prefix(c, prompt, images), false);
+        });
+        return m;
     }
 
-    size_t budget_ = 0, slots_ = 0, parked_bytes_ = 0, evictions_ = 0;
+    size_t budget_ = 0, slots_ = 0, parked_ = 0, evictions_ = 0;
     uint64_t clock_ = 0;
-    std::deque<SavedConversation> entries_;   // park order, oldest first
-    std::vector<uint64_t> stamps_;            // entries_[i]'s last use
-    ConversationKvReuse retained_;
+    std::vector<Parked> shelf_;   // park order, oldest first
+    ConversationKvReuse kept_;    // the K/V of the last mount, for an incremental re-park
 };
 
 }  // namespace strata::core

@@ -1,10 +1,16 @@
 // conversation_state.cpp - running-state checkpoints and whole-session snapshots
-// (include/strata_kv/conversation_snapshot.hpp; the reference's src/core/conversation_state.cpp:180-507).
+// (include/strata_kv/conversation_snapshot.hpp; the C++ API of the reference's src/core/conversation_state.cpp).
 //
-// Validation and sizing follow the reference's rules (every stage, every checkpoint and the draft are checked
-// before the first byte moves; byte estimates count exactly what the image will hold).  Movement is batched per
-// device: a park of the main session is ONE transfer batch (running state + every owned layer's K/V: one or two
-// gather launches, the device->host copies, one synchronisation), then the draft's device, then each stage's.
+// Accounting and refusals.  Every question this file answers about a session - can it hold a branch of T tokens,
+// how big is its share of an image, does an image's running state fit it - is read off ONE plan of that session's
+// running state (RunningState, built by running_state) and summed in ONE checked byte ledger (Ledger).  Sizing
+// adds plan entries to a ledger, validation compares an image's buffers with the same entries, and a save sizes
+// its buffers from them, so the three cannot disagree about a buffer.  The refusal set is the reference's: any
+// failed check refuses the whole call before the first byte moves.  The reasons are this file's own words.
+//
+// Movement is batched per device: a park of the main session is ONE transfer batch (running state + every owned
+// layer's K/V: one or two gather launches, the device->host copies, one synchronisation), then the draft's device,
+// then each later stage's.
 #include "snapshot_detail.hpp"
 
 #include <cuda_runtime.h>
@@ -42,161 +48,164 @@ size_t owned_count(const SessionState& ss) { return (size_t) std::max<int64_t>(s
 const QsaState& owned_layer(const SessionState& ss, size_t j) { return ss.qsa_states[(size_t) ss.qsa_ord0 + j]; }
 int64_t stage_count(const ConversationStageSet& s) { return s.empty() ? 0 : s.count; }
 
-/// Image starts strictly increasing and inside the token range.
+namespace {
+
+/// A byte total that goes sour on the first overflowing or invalid term and stays sour.
+class Ledger {
+public:
+    /// `count` entries of `each` bytes.
+    Ledger& add(uint64_t count, uint64_t each) {
+        size_t n = 0;
+        if (!checked_product(n, {count, each})) ok_ = false;
+        return add(n);
+    }
+    Ledger& add(size_t n) {
+        if (ok_ && !checked_add(total_, n)) ok_ = false;
+        return *this;
+    }
+    /// A term whose 0 means "invalid" (a K/V estimate of a layer that cannot be parked).
+    Ledger& add_estimate(size_t n) {
+        if (n == 0) ok_ = false;
+        return add(n);
+    }
+    bool ok() const { return ok_; }
+    size_t total() const { return total_; }
+
+private:
+    size_t total_ = 0;
+    bool ok_ = true;
+};
+
+/// Why one owned QSA layer's indexer cannot carry a `tokens`-long branch (its buffers, its cell capacity, the
+/// pooled rows the branch fills plus the spare row the next block pools into), or null when it can.
+const char* indexer_fault(const QsaState& st, const ModelGeometry& g, uint64_t tokens) {
+    if (!st.idx_tail || !st.idx_dead || !st.idx_block_pos || !st.idx_pooled) return "an indexer buffer is missing";
+    if (st.max_cells < 0 || tokens > (uint64_t) st.max_cells) return "a QSA layer holds fewer cells than the branch";
+    const uint64_t rows_used = tokens / (uint64_t) strata::kernels::qsa_real_shapes().idx_block;
+    if (tokens > 0 && rows_used + 1 > (uint64_t) std::max<int64_t>(st.idx_pooled_rows, 0))
+        return "the indexer has no spare pooled row past the branch";
+    size_t pooled = 0;
+    if (!checked_product(pooled, {rows_used + 1, (uint64_t) g.idx_key_dim, sizeof(float)}))
+        return "the indexer's pooled rows overflow a byte count";
+    return nullptr;
+}
+
+/// Why checkpoint `c` cannot sit beside the live branch of `view` in an image with `stages` later stages, as far
+/// as its own shape tells (the running-state sizes are checked against the sessions separately), or null.
+const char* checkpoint_shape_fault(const ConversationCheckpoint& c, const ConversationView& view, int64_t stages) {
+    const bool live_prefix = !c.ids.empty() && c.ids.size() <= view.ids.size() &&
+                             std::equal(c.ids.begin(), c.ids.end(), view.ids.begin());
+    if (!live_prefix) return "a retained checkpoint is not a prefix of the live branch";
+    if ((int64_t) c.stage_parts.size() != stages)
+        return stages ? "a retained checkpoint lacks a part for every later stage"
+                      : "a retained checkpoint carries stage parts but the session is not split";
+    for (const ConversationCheckpoint& part : c.stage_parts)
+        if (part.ids.size() != c.ids.size() || !part.imgs.empty() || !part.stage_parts.empty())
+            return "a checkpoint's stage part does not cover exactly the checkpoint's tokens";
+    if (!conversation_match_detail::images_agree(c, view.images, c.ids.size()))
+        return "a retained checkpoint's images are not the live branch's images over its tokens";
+    return nullptr;
+}
+
+/// A session's share of an image of an `upto`-token branch: its running state, the token ids, the K/V directory
+/// and every owned layer's K/V, and `draft` (the main session's draft layer) when given.
+bool add_session_share(Ledger& ledger, const SessionState& ss, const ModelGeometry& g, int64_t upto,
+                       const QsaState* draft, std::string& error) {
+    RunningState rs;
+    if (!running_state(ss, g, (size_t) upto, rs, error)) return false;
+    ledger.add(rs.gdn()).add(rs.ple()).add(rs.tails()).add(rs.dead()).add(rs.block_pos());
+    ledger.add((uint64_t) upto, sizeof(int32_t));
+    ledger.add(rs.layers + (draft ? 1 : 0), sizeof(ConversationKv));
+    for (size_t j = 0; j < rs.layers; ++j) ledger.add_estimate(conversation_kv_bytes(owned_layer(ss, j), g, upto, true));
+    if (draft) ledger.add_estimate(conversation_kv_bytes(*draft, g, upto, false));
+    return true;
+}
+
+/// What a copy of retained checkpoint `c` adds to an image (its own vectors and, recursively, its stage parts).
+void add_checkpoint_copy(Ledger& ledger, const ConversationCheckpoint& c) {
+    ledger.add(c.ids.size(), sizeof(int32_t)).add(c.imgs.size(), sizeof(ConversationImageKey));
+    for (const std::vector<uint8_t>* v : {&c.gdn, &c.ple, &c.tails, &c.dead, &c.block_pos}) ledger.add(v->size());
+    ledger.add(c.stage_parts.capacity(), sizeof(ConversationCheckpoint));
+    for (const ConversationCheckpoint& part : c.stage_parts) add_checkpoint_copy(ledger, part);
+}
+
+}  // namespace
+
 bool images_ordered(const std::vector<ConversationImageKey>& images, size_t tokens) {
-    int64_t last = -1;
-    for (const auto& im : images) {
-        if (im.start < 0 || im.start <= last || (uint64_t) im.start >= tokens) return false;
-        last = im.start;
+    for (size_t i = 0; i < images.size(); ++i) {
+        const int64_t start = images[i].start;
+        if (start < 0 || (uint64_t) start >= tokens || (i > 0 && start <= images[i - 1].start)) return false;
     }
     return true;
 }
 
-/// The session can hold a `tokens`-long running state: sizes, pointers, indexer capacity.
-bool running_targets(const SessionState& ss, const ModelGeometry& g, size_t tokens, ConversationStateSizes& z,
-                     std::string& error) {
-    if (!conversation_session_sizes(g, ss, z, error)) return false;
-    if (ss.max_cells < 0 || tokens > (uint64_t) ss.max_cells || (z.gdn && !ss.gdn_state) ||
-        (owned_count(ss) && !ss.qsa_states))
-        return fail(error, "invalid session running-state targets");
-    const uint64_t block = (uint64_t) strata::kernels::qsa_real_shapes().idx_block;
-    for (size_t j = 0; j < owned_count(ss); ++j) {
-        const QsaState& st = owned_layer(ss, j);
-        size_t pooled = 0;
-        if (!st.idx_tail || !st.idx_dead || !st.idx_block_pos || !st.idx_pooled || st.max_cells < 0 ||
-            tokens > (uint64_t) st.max_cells ||
-            (tokens && tokens / block >= (uint64_t) std::max<int64_t>(0, st.idx_pooled_rows)) ||
-            !checked_product(pooled, {tokens / block + 1, (uint64_t) g.idx_key_dim, sizeof(float)}))
-            return fail(error, "invalid indexer running-state target");
-    }
+bool running_state(const SessionState& ss, const ModelGeometry& g, size_t tokens, RunningState& rs,
+                   std::string& error) {
+    rs = {};
+    if (!conversation_session_sizes(g, ss, rs.per, error)) return false;
+    rs.layers = owned_count(ss);
+    rs.keeps_ple = ss.ple_hist != nullptr;
+    if (ss.max_cells < 0 || tokens > (uint64_t) ss.max_cells)
+        return fail(error, "the session holds fewer cells than the branch");
+    if ((rs.per.gdn && !ss.gdn_state) || (rs.layers && !ss.qsa_states))
+        return fail(error, "the session lacks a running-state buffer its carve needs");
+    for (size_t j = 0; j < rs.layers; ++j)
+        if (const char* why = indexer_fault(owned_layer(ss, j), g, tokens)) return fail(error, why);
     return true;
 }
 
-/// The main session plus the stages tile [0, n_layers) in order, each stage's carve consistent.
 bool stages_tile(const ConversationStageSet& stages, const SessionState& main_ss, const ModelGeometry& g,
                  std::string& error) {
     if (stages.empty()) return true;
     if (stages.count > (int64_t) (std::numeric_limits<size_t>::max() / sizeof(ConversationStageSnapshot)))
-        return fail(error, "too many layer-split stages");
-    const int64_t n_qsa = g.n_qsa_layers();
-    int64_t next = main_ss.layer_hi;
+        return fail(error, "the stage set is larger than an image can index");
+    const int64_t n_qsa = g.n_qsa_layers(), interval = std::max<int64_t>(g.qsa_interval, 1);
+    int64_t covered = main_ss.layer_hi;   // the layers [0, covered) belong to the main session and earlier stages
     for (int64_t i = 0; i < stages.count; ++i) {
         const SessionState* ss = stages.stages[i].session;
-        if (!ss) return fail(error, "layer-split stage has no session");
-        ConversationStateSizes z;
-        if (!conversation_session_sizes(g, *ss, z, error)) return false;
-        if (ss->layer_lo != next || ss->layer_lo >= ss->layer_hi || ss->layer_hi > g.n_layers)
-            return fail(error, "layer-split stages do not tile the model");
-        if (ss->qsa_ord0 < ss->layer_lo / std::max<int64_t>(g.qsa_interval, 1))
-            return fail(error, "layer-split stage carve starts before its layer range");
-        if (ss->qsa_alloc > n_qsa - ss->qsa_ord0) return fail(error, "layer-split stage carve past the last QSA layer");
-        next = ss->layer_hi;
+        if (!ss) return fail(error, "a later stage has no session");
+        ConversationStateSizes unused;
+        if (!conversation_session_sizes(g, *ss, unused, error)) return false;
+        if (ss->layer_lo != covered || ss->layer_hi <= ss->layer_lo || ss->layer_hi > g.n_layers)
+            return fail(error, "the later stages do not continue the layer range in order");
+        if (ss->qsa_ord0 < ss->layer_lo / interval || ss->qsa_alloc > n_qsa - ss->qsa_ord0)
+            return fail(error, "a later stage's QSA carve lies outside its layers");
+        covered = ss->layer_hi;
     }
-    if (next != g.n_layers) return fail(error, "layer-split stages do not cover the whole model");
+    if (covered != g.n_layers) return fail(error, "the later stages stop short of the last layer");
     return true;
 }
 
-/// A later stage's share of a snapshot estimate.
-bool stage_estimate(const SessionState& ss, const ModelGeometry& g, int64_t upto, size_t& total, std::string& error) {
-    ConversationStateSizes z;
-    if (!conversation_session_sizes(g, ss, z, error) || !running_targets(ss, g, (size_t) upto, z, error)) return false;
-    const size_t layers = owned_count(ss);
-    size_t dir = 0, tails = 0, dead = 0, pos = 0, ids = 0;
-    if (!checked_product(dir, {layers, sizeof(ConversationKv)}) || !checked_product(tails, {layers, z.tail}) ||
-        !checked_product(dead, {layers, z.dead}) || !checked_product(pos, {layers, z.block_pos}) ||
-        !checked_product(ids, {(uint64_t) upto, sizeof(int32_t)}))
-        return fail(error, "stage byte count overflow");
-    for (size_t n : {dir, ids, tails, dead, pos, z.gdn, ss.ple_hist ? z.ple : (size_t) 0})
-        if (!checked_add(total, n)) return fail(error, "stage byte count overflow");
-    for (size_t j = 0; j < layers; ++j) {
-        const size_t n = conversation_kv_bytes(owned_layer(ss, j), g, upto, true);
-        if (!n || !checked_add(total, n)) return fail(error, "invalid or overflowing stage K/V byte estimate");
-    }
-    return true;
-}
-
-/// The live branch and every retained checkpoint are prefixes of it, with the right per-stage parts.
 bool view_ok(const ConversationView& view, const SessionState& ss, const ConversationStageSet& stages,
              const ModelGeometry& g, std::string& error) {
-    ConversationStateSizes z;
-    if (!running_targets(ss, g, view.ids.size(), z, error)) return false;
-    if (view.ids.empty() || !images_ordered(view.images, view.ids.size()) ||
-        std::any_of(view.ids.begin(), view.ids.end(), [](int32_t id) { return id < 0; }))
-        return fail(error, "invalid live token/image metadata");
-    for (const auto& c : view.checkpoints) {
-        if (c.ids.empty() || c.ids.size() > view.ids.size() || !std::equal(c.ids.begin(), c.ids.end(), view.ids.begin()))
-            return fail(error, "checkpoint is not a live token prefix");
-        if ((int64_t) c.stage_parts.size() != stage_count(stages))
-            return fail(error, stages.empty() ? "layer-split parking is not supported"
-                                              : "checkpoint is missing a layer-split stage part");
+    RunningState rs;
+    if (!running_state(ss, g, view.ids.size(), rs, error)) return false;
+    if (view.ids.empty()) return fail(error, "the live branch is empty");
+    if (std::any_of(view.ids.begin(), view.ids.end(), [](int32_t id) { return id < 0; }))
+        return fail(error, "the live branch has a negative token id");
+    if (!images_ordered(view.images, view.ids.size()))
+        return fail(error, "the live branch's images are out of order or past its tokens");
+    const int64_t n_stages = stage_count(stages);
+    for (const ConversationCheckpoint& c : view.checkpoints) {
+        if (const char* why = checkpoint_shape_fault(c, view, n_stages)) return fail(error, why);
         if (!conversation_checkpoint_validate(c, ss, g, error)) return false;
-        for (size_t i = 0; i < c.stage_parts.size(); ++i) {
-            const ConversationCheckpoint& part = c.stage_parts[i];
-            if (part.ids.size() != c.ids.size() || !part.imgs.empty() || !part.stage_parts.empty())
-                return fail(error, "layer-split checkpoint part is not a live token prefix");
-            if (!conversation_checkpoint_validate(part, *stages.stages[i].session, g, error)) return false;
-        }
-        size_t k = 0;
-        for (const auto& key : view.images) {
-            if ((uint64_t) key.start >= c.ids.size()) break;
-            if (k >= c.imgs.size() || !(c.imgs[k++] == key)) return fail(error, "checkpoint image identity differs");
-        }
-        if (k != c.imgs.size()) return fail(error, "checkpoint image prefix differs");
+        for (int64_t i = 0; i < n_stages; ++i)
+            if (!conversation_checkpoint_validate(c.stage_parts[(size_t) i], *stages.stages[i].session, g, error))
+                return false;
     }
     return true;
 }
 
-bool checkpoint_meta_bytes(const ConversationCheckpoint& c, size_t& total) {
-    size_t ids = 0, imgs = 0, parts = 0;
-    if (!checked_product(ids, {c.ids.size(), sizeof(int32_t)}) ||
-        !checked_product(imgs, {c.imgs.size(), sizeof(ConversationImageKey)}))
-        return false;
-    for (size_t n : {ids, imgs, c.gdn.size(), c.ple.size(), c.tails.size(), c.dead.size(), c.block_pos.size()})
-        if (!checked_add(total, n)) return false;
-    if (!checked_product(parts, {c.stage_parts.capacity(), sizeof(ConversationCheckpoint)}) || !checked_add(total, parts))
-        return false;
-    for (const auto& p : c.stage_parts)
-        if (!checkpoint_meta_bytes(p, total)) return false;
-    return true;
-}
-
-/// The main session's share: its running state, metadata, every owned layer's K/V and the draft's.
-bool main_estimate(const ConversationView& view, const SessionState& ss, const ModelGeometry& g, const QsaState& draft,
-                   size_t& bytes, std::string& error) {
-    ConversationStateSizes z;
-    if (!conversation_session_sizes(g, ss, z, error)) return false;
-    const uint64_t qsa = owned_count(ss);
-    size_t ids = 0, imgs = 0, cps = 0, layers = 0, tails = 0, dead = 0, pos = 0;
-    if (!checked_product(ids, {view.ids.size(), sizeof(int32_t)}) ||
-        !checked_product(imgs, {view.images.size(), sizeof(ConversationImageKey)}) ||
-        !checked_product(cps, {view.checkpoints.size(), sizeof(ConversationCheckpoint)}) ||
-        !checked_product(layers, {qsa + 1, sizeof(ConversationKv)}) || !checked_product(tails, {qsa, z.tail}) ||
-        !checked_product(dead, {qsa, z.dead}) || !checked_product(pos, {qsa, z.block_pos}))
-        return fail(error, "snapshot metadata byte count overflow");
-    for (size_t n : {ids, imgs, cps, layers, tails, dead, pos, z.gdn, ss.ple_hist ? z.ple : (size_t) 0})
-        if (!checked_add(bytes, n)) return fail(error, "snapshot byte count overflow");
-    for (const auto& c : view.checkpoints)
-        if (!checkpoint_meta_bytes(c, bytes)) return fail(error, "checkpoint byte count overflow");
-    const int64_t upto = (int64_t) view.ids.size();
-    for (uint64_t i = 0; i <= qsa; ++i) {
-        const QsaState& st = i == qsa ? draft : owned_layer(ss, (size_t) i);
-        const size_t n = conversation_kv_bytes(st, g, upto, i != qsa);
-        if (!n || !checked_add(bytes, n)) return fail(error, "invalid or overflowing K/V byte estimate");
-    }
-    return true;
-}
-
-/// Queue a checkpoint's running state (save direction) into `t`.
+/// Queue a checkpoint's running state (save direction) into `t`, its buffers sized from the session's plan.
 bool enqueue_checkpoint_save(ConversationCheckpoint& c, const SessionState& ss, const ModelGeometry& g,
                              strata::kv::Transfer& t, std::string& error) {
-    ConversationStateSizes z;
-    if (!running_targets(ss, g, c.ids.size(), z, error)) return false;
-    const size_t layers = owned_count(ss);
-    c.gdn.resize(z.gdn);
-    c.ple.resize(ss.ple_hist ? z.ple : 0);
-    c.tails.resize(layers * z.tail);
-    c.dead.resize(layers * z.dead);
-    c.block_pos.resize(layers * z.block_pos);
+    RunningState rs;
+    if (!running_state(ss, g, c.ids.size(), rs, error)) return false;
+    c.gdn.resize(rs.gdn());
+    c.ple.resize(rs.ple());
+    c.tails.resize(rs.tails());
+    c.dead.resize(rs.dead());
+    c.block_pos.resize(rs.block_pos());
     auto dev = [](const void* p) {
         strata::kv::DeviceStream s;
         s.base = p;
@@ -204,11 +213,12 @@ bool enqueue_checkpoint_save(ConversationCheckpoint& c, const SessionState& ss, 
     };
     if (!c.gdn.empty()) t.save(dev(ss.gdn_state), 0, c.gdn.size(), c.gdn.data());
     if (!c.ple.empty()) t.save(dev(ss.ple_hist), 0, c.ple.size(), c.ple.data());
-    for (size_t j = 0; j < layers; ++j) {
+    const ConversationStateSizes& per = rs.per;
+    for (size_t j = 0; j < rs.layers; ++j) {
         const QsaState& st = owned_layer(ss, j);
-        t.save(dev(st.idx_tail), 0, z.tail, c.tails.data() + j * z.tail);
-        t.save(dev(st.idx_dead), 0, z.dead, c.dead.data() + j * z.dead);
-        t.save(dev(st.idx_block_pos), 0, z.block_pos, c.block_pos.data() + j * z.block_pos);
+        t.save(dev(st.idx_tail), 0, per.tail, c.tails.data() + j * per.tail);
+        t.save(dev(st.idx_dead), 0, per.dead, c.dead.data() + j * per.dead);
+        t.save(dev(st.idx_block_pos), 0, per.block_pos, c.block_pos.data() + j * per.block_pos);
     }
     return true;
 }
@@ -221,25 +231,28 @@ using namespace snapshot_detail;
 
 bool conversation_state_sizes(const ModelGeometry& g, ConversationStateSizes& z, std::string& error) {
     z = {};
-    const auto key = geometry_key(g);
-    for (size_t i = 0; i < key.size(); ++i)
-        if (key[i] < 0 || (i != 1 && key[i] == 0)) return fail(error, "invalid model geometry");
-    size_t recurrence = 0, convolution = 0;
-    if (!checked_product(recurrence, {(uint64_t) g.ssm_state_size, (uint64_t) g.ssm_v_heads, (uint64_t) g.ssm_state_size}) ||
-        !checked_product(convolution, {(uint64_t) g.ssm_conv_channels, (uint64_t) (g.ssm_d_conv - 1)}) ||
-        !checked_add(recurrence, convolution) ||
-        !checked_product(z.gdn, {(uint64_t) g.n_gdn_layers(), recurrence, sizeof(float)}) ||
-        !checked_product(z.ple, {(uint64_t) strata::kernels::NG_HIST, (uint64_t) strata::kernels::NG_HC_DIM, sizeof(float)}) ||
-        !checked_product(z.tail, {(uint64_t) (strata::kernels::qsa_real_shapes().idx_block - 1), (uint64_t) g.idx_key_dim,
-                                  sizeof(float)}) ||
-        !checked_product(z.dead, {(uint64_t) g.idx_key_dim, sizeof(float)}))
-        return fail(error, "running-state byte count overflow");
+    std::array<int64_t, 18> dims = geometry_key(g);
+    const int64_t layers = dims[1];
+    dims[1] = 1;   // a geometry may have no layers; every other dimension must be positive
+    if (layers < 0 || *std::min_element(dims.begin(), dims.end()) <= 0)
+        return fail(error, "the model geometry has a non-positive dimension");
+    const uint64_t idx_block = (uint64_t) strata::kernels::qsa_real_shapes().idx_block;
+    size_t state = 0, conv = 0, row = 0;
+    bool ok = checked_product(state, {(uint64_t) g.ssm_state_size, (uint64_t) g.ssm_v_heads, (uint64_t) g.ssm_state_size}) &&
+              checked_product(conv, {(uint64_t) g.ssm_conv_channels, (uint64_t) (g.ssm_d_conv - 1)});
+    row = state;
+    ok = ok && checked_add(row, conv) &&
+         checked_product(z.gdn, {(uint64_t) g.n_gdn_layers(), row, sizeof(float)}) &&
+         checked_product(z.ple, {(uint64_t) strata::kernels::NG_HIST, (uint64_t) strata::kernels::NG_HC_DIM, sizeof(float)}) &&
+         checked_product(z.tail, {idx_block - 1, (uint64_t) g.idx_key_dim, sizeof(float)}) &&
+         checked_product(z.dead, {(uint64_t) g.idx_key_dim, sizeof(float)});
     z.block_pos = sizeof(int32_t);
-    size_t all = 0;
-    if (!checked_product(all, {(uint64_t) g.n_qsa_layers(), z.tail}) ||
-        !checked_product(all, {(uint64_t) g.n_qsa_layers(), z.dead}) ||
-        !checked_product(all, {(uint64_t) g.n_qsa_layers(), z.block_pos}))
-        return fail(error, "indexer byte count overflow");
+    // every QSA layer's share must be countable too (a full carve owns all of them)
+    size_t whole = 0;
+    const uint64_t n_qsa = (uint64_t) g.n_qsa_layers();
+    ok = ok && checked_product(whole, {n_qsa, z.tail}) && checked_product(whole, {n_qsa, z.dead}) &&
+         checked_product(whole, {n_qsa, z.block_pos});
+    if (!ok) return fail(error, "the running state's byte counts overflow");
     return true;
 }
 
@@ -247,9 +260,10 @@ bool conversation_session_sizes(const ModelGeometry& g, const SessionState& ss, 
                                 std::string& error) {
     if (!conversation_state_sizes(g, z, error)) return false;
     const int64_t n_gdn = g.n_gdn_layers(), n_qsa = g.n_qsa_layers();
-    if (ss.gdn_alloc < 0 || ss.gdn_alloc > n_gdn || ss.qsa_ord0 < 0 || ss.qsa_alloc < 0 || ss.qsa_ord0 > n_qsa ||
-        ss.qsa_alloc > n_qsa - ss.qsa_ord0)
-        return fail(error, "invalid session layer carve");
+    const bool gdn_carve = 0 <= ss.gdn_alloc && ss.gdn_alloc <= n_gdn;
+    const bool qsa_carve = 0 <= ss.qsa_ord0 && ss.qsa_ord0 <= n_qsa && 0 <= ss.qsa_alloc && ss.qsa_alloc <= n_qsa - ss.qsa_ord0;
+    if (!gdn_carve || !qsa_carve) return fail(error, "the session's layer carve lies outside the model");
+    // the GDN rows are per layer: a session carries only the rows of the layers it owns
     z.gdn = n_gdn > 0 ? z.gdn / (size_t) n_gdn * (size_t) ss.gdn_alloc : 0;
     return true;
 }
@@ -263,13 +277,13 @@ bool conversation_checkpoint_validate(const ConversationCheckpoint& c, const Ses
 
 bool snapshot_detail::checkpoint_validate_sized(const ConversationCheckpoint& c, const SessionState& ss,
                                                 const ModelGeometry& g, std::string& error, const SizeOf& size_of) {
-    ConversationStateSizes z;
-    if (!running_targets(ss, g, c.ids.size(), z, error)) return false;
-    const size_t layers = owned_count(ss);
-    auto n = [&](const std::vector<uint8_t>& v) { return size_of(&v, v.size()); };
-    if (n(c.gdn) != z.gdn || n(c.ple) != (ss.ple_hist ? z.ple : 0) || n(c.tails) != layers * z.tail ||
-        n(c.dead) != layers * z.dead || n(c.block_pos) != layers * z.block_pos || !images_ordered(c.imgs, c.ids.size()))
-        return fail(error, "invalid checkpoint running-state payload");
+    RunningState rs;
+    if (!running_state(ss, g, c.ids.size(), rs, error)) return false;
+    auto holds = [&](const std::vector<uint8_t>& v, size_t want) { return size_of(&v, v.size()) == want; };
+    if (!holds(c.gdn, rs.gdn()) || !holds(c.ple, rs.ple()) || !holds(c.tails, rs.tails()) || !holds(c.dead, rs.dead()) ||
+        !holds(c.block_pos, rs.block_pos()))
+        return fail(error, "a checkpoint's running-state buffers are not the size the session needs");
+    if (!images_ordered(c.imgs, c.ids.size())) return fail(error, "a checkpoint's images are out of order or past its tokens");
     return true;
 }
 
@@ -283,8 +297,8 @@ bool conversation_checkpoint_save(ConversationCheckpoint& c, const SessionState&
 bool conversation_checkpoint_restore(const ConversationCheckpoint& c, SessionState& ss, const ModelGeometry& g,
                                      std::string& error) {
     if (!conversation_checkpoint_validate(c, ss, g, error)) return false;
-    ConversationStateSizes z;
-    if (!conversation_session_sizes(g, ss, z, error)) return false;
+    RunningState rs;
+    if (!running_state(ss, g, c.ids.size(), rs, error)) return false;
     auto dev = [](const void* p) {
         strata::kv::DeviceStream s;
         s.base = p;
@@ -293,22 +307,24 @@ bool conversation_checkpoint_restore(const ConversationCheckpoint& c, SessionSta
     strata::kv::Transfer t;
     if (!c.gdn.empty()) t.restore(c.gdn.data(), 0, c.gdn.size(), dev(ss.gdn_state));
     if (!c.ple.empty()) t.restore(c.ple.data(), 0, c.ple.size(), dev(ss.ple_hist));
-    const uint64_t block = (uint64_t) strata::kernels::qsa_real_shapes().idx_block;
-    for (size_t j = 0; j < owned_count(ss); ++j) {
+    const ConversationStateSizes& per = rs.per;
+    // the pooled row the next indexer block accumulates into starts as the dead key again
+    const size_t spare_row = c.ids.size() / (size_t) strata::kernels::qsa_real_shapes().idx_block;
+    for (size_t j = 0; j < rs.layers; ++j) {
         const QsaState& st = owned_layer(ss, j);
-        t.restore(c.tails.data() + j * z.tail, 0, z.tail, dev(st.idx_tail));
-        t.restore(c.dead.data() + j * z.dead, 0, z.dead, dev(st.idx_dead));
-        t.restore(c.block_pos.data() + j * z.block_pos, 0, z.block_pos, dev(st.idx_block_pos));
-        if (!c.ids.empty()) {
-            // the indexer's moving spare row is the dead key again (the row the next block will pool into)
-            const size_t row = c.ids.size() / block;
-            t.restore(c.dead.data() + j * z.dead, 0, z.dead, dev(st.idx_pooled + row * (size_t) g.idx_key_dim));
-        }
+        const uint8_t* dead = c.dead.data() + j * per.dead;
+        t.restore(c.tails.data() + j * per.tail, 0, per.tail, dev(st.idx_tail));
+        t.restore(dead, 0, per.dead, dev(st.idx_dead));
+        t.restore(c.block_pos.data() + j * per.block_pos, 0, per.block_pos, dev(st.idx_block_pos));
+        if (!c.ids.empty()) t.restore(dead, 0, per.dead, dev(st.idx_pooled + spare_row * (size_t) g.idx_key_dim));
     }
     if (!t.run(error, "conversation snapshot running-state copy")) return false;
+    // the PLE history's two previous tokens are the branch's last two ids, oldest first (-1 before the start)
     const size_t n = c.ids.size();
-    ss.ple_prev[0] = n >= 2 ? c.ids[n - 2] : -1;
-    ss.ple_prev[1] = n >= 1 ? c.ids[n - 1] : -1;
+    for (size_t k = 0; k < 2; ++k) {
+        const size_t back = 2 - k;
+        ss.ple_prev[k] = n >= back ? c.ids[n - back] : -1;
+    }
     return device_sync(error);
 }
 
@@ -317,16 +333,17 @@ bool conversation_checkpoint_restore(const ConversationCheckpoint& c, SessionSta
 bool conversation_snapshot_bytes(const ConversationView& view, const SessionState& ss, const ConversationStageSet& stages,
                                  const ModelGeometry& g, const QsaState& draft, size_t& bytes, std::string& error) {
     bytes = 0;
-    if (!stages_tile(stages, ss, g, error) || !view_ok(view, ss, stages, g, error) ||
-        !main_estimate(view, ss, g, draft, bytes, error))
-        return false;
-    if (!stages.empty()) {
-        size_t dir = 0;
-        if (!checked_product(dir, {(uint64_t) stages.count, sizeof(ConversationStageSnapshot)}) || !checked_add(bytes, dir))
-            return fail(error, "layer-split stage directory overflow");
-    }
+    if (!stages_tile(stages, ss, g, error) || !view_ok(view, ss, stages, g, error)) return false;
+    const int64_t upto = (int64_t) view.ids.size();
+    Ledger ledger;
+    if (!add_session_share(ledger, ss, g, upto, &draft, error)) return false;
+    ledger.add(view.images.size(), sizeof(ConversationImageKey)).add(view.checkpoints.size(), sizeof(ConversationCheckpoint));
+    for (const ConversationCheckpoint& c : view.checkpoints) add_checkpoint_copy(ledger, c);
+    if (!stages.empty()) ledger.add((uint64_t) stages.count, sizeof(ConversationStageSnapshot));
     for (int64_t i = 0; i < stage_count(stages); ++i)
-        if (!stage_estimate(*stages.stages[i].session, g, (int64_t) view.ids.size(), bytes, error)) return false;
+        if (!add_session_share(ledger, *stages.stages[i].session, g, upto, nullptr, error)) return false;
+    if (!ledger.ok()) return fail(error, "the snapshot's byte count overflows, or a layer's K/V cannot be sized");
+    bytes = ledger.total();
     return true;
 }
 
@@ -341,24 +358,27 @@ bool conversation_snapshot_capture_bytes(const ConversationKvReuse& reuse, const
                                          std::string& error) {
     if (!conversation_snapshot_bytes(view, ss, stages, g, draft, bytes, error)) return false;
     if (reuse.kv.empty()) return true;
-    const size_t layers = owned_count(ss) + 1;   // the main session's layers and the draft; never a stage's
-    if (reuse.kv.size() != layers || reuse.unchanged_tokens < 0 || reuse.unchanged_tokens > reuse.captured_tokens ||
-        reuse.unchanged_tokens > (int64_t) view.ids.size())
-        return fail(error, "invalid retained K/V prefix");
-    for (size_t i = 0; i < layers; ++i) {
-        const bool index = i + 1 != layers;
-        const QsaState& st = index ? owned_layer(ss, i) : draft;
-        if (!conversation_kv_validate(reuse.kv[i], st, g, reuse.captured_tokens, index, error)) return false;
-        const size_t fresh = conversation_kv_bytes(st, g, (int64_t) view.ids.size(), index);
-        size_t retained = 0;
-        if (!conversation_kv_capture_bytes(reuse.kv[i], st, g, (int64_t) view.ids.size(), index, retained, error))
-            return false;
-        bytes -= fresh;
-        if (!checked_add(bytes, retained)) return fail(error, "retained K/V allocation overflow");
+    // only the main session's layers and its draft are ever reused, never a later stage's
+    const size_t reused = owned_count(ss) + 1;
+    const int64_t upto = (int64_t) view.ids.size();
+    const bool prefix_ok = reuse.kv.size() == reused && reuse.unchanged_tokens >= 0 &&
+                           reuse.unchanged_tokens <= reuse.captured_tokens && reuse.unchanged_tokens <= upto;
+    if (!prefix_ok) return fail(error, "the retained K/V does not describe a prefix of this session's layers");
+    // each reused layer's fresh estimate gives way to what its retained buffers grow to
+    size_t rest = bytes;
+    Ledger grown;
+    for (size_t i = 0; i < reused; ++i) {
+        const bool is_draft = i + 1 == reused;
+        const QsaState& st = is_draft ? draft : owned_layer(ss, i);
+        if (!conversation_kv_validate(reuse.kv[i], st, g, reuse.captured_tokens, !is_draft, error)) return false;
+        size_t kept = 0;
+        if (!conversation_kv_capture_bytes(reuse.kv[i], st, g, upto, !is_draft, kept, error)) return false;
+        rest -= conversation_kv_bytes(st, g, upto, !is_draft);
+        grown.add(kept);
     }
-    size_t dir = 0;
-    if (!checked_product(dir, {reuse.kv.capacity() - layers, sizeof(ConversationKv)}) || !checked_add(bytes, dir))
-        return fail(error, "retained K/V directory overflow");
+    grown.add(reuse.kv.capacity() - reused, sizeof(ConversationKv)).add(rest);
+    if (!grown.ok()) return fail(error, "the capture's byte count overflows");
+    bytes = grown.total();
     return true;
 }
 
@@ -440,39 +460,46 @@ bool conversation_snapshot_validate(const SavedConversation& image, const Sessio
     return snapshot_validate_sized(image, ss, stages, g, draft, error, own_size);
 }
 
+namespace {
+/// One session's part of an image fits that session: its running-state checkpoint, and one K/V image per owned
+/// layer (then the draft's, for the main session) each valid for its layer at `upto` tokens.
+bool session_part_fits(const ConversationCheckpoint& state, const std::vector<ConversationKv>& kv,
+                       const SessionState& ss, const QsaState* draft, const ModelGeometry& g, int64_t upto,
+                       std::string& error, const SizeOf& size_of) {
+    if (!checkpoint_validate_sized(state, ss, g, error, size_of)) return false;
+    const size_t layers = owned_count(ss);
+    if (kv.size() != layers + (draft ? 1 : 0)) return fail(error, "the image holds another number of K/V layers than the session");
+    for (size_t j = 0; j < layers; ++j)
+        if (!kv_validate_sized(kv[j], owned_layer(ss, j), g, upto, true, error, size_of)) return false;
+    return !draft || kv_validate_sized(kv.back(), *draft, g, upto, false, error, size_of);
+}
+}  // namespace
+
 bool snapshot_detail::snapshot_validate_sized(const SavedConversation& image, const SessionState& ss,
                                               const ConversationStageSet& stages, const ModelGeometry& g,
                                               const QsaState& draft, std::string& error, const SizeOf& size_of) {
     if (!stages_tile(stages, ss, g, error)) return false;
-    if (!image.live.stage_parts.empty()) return fail(error, "layer-split parking is not supported");
-    if ((int64_t) image.stage_parts.size() != stage_count(stages))
-        return fail(error, stages.empty() ? "layer-split parking is not supported"
-                                          : "snapshot is missing a layer-split stage part");
-    if (image.geometry != geometry_key(g)) return fail(error, "incompatible runtime geometry");
+    const int64_t n_stages = stage_count(stages);
+    if (!image.live.stage_parts.empty() || (int64_t) image.stage_parts.size() != n_stages)
+        return fail(error, n_stages ? "the image lacks a part for every later stage"
+                                    : "the image was parked from a split session and this one is not split");
+    if (image.geometry != geometry_key(g)) return fail(error, "the image was parked under another model geometry");
     if (image.layer_lo != ss.layer_lo || image.layer_hi != ss.layer_hi)
-        return fail(error, "snapshot from another session layer range");
+        return fail(error, "the image covers other layers than the session");
     const ConversationView view{image.live.ids, image.live.imgs, image.checkpoints, image.cvec};
-    if (!view_ok(view, ss, stages, g, error) || !checkpoint_validate_sized(image.live, ss, g, error, size_of))
-        return false;
-    const size_t layers = owned_count(ss);
-    if (image.kv.size() != layers + 1) return fail(error, "invalid K/V layer count");
     const int64_t upto = (int64_t) image.live.ids.size();
-    for (size_t j = 0; j < layers; ++j)
-        if (!kv_validate_sized(image.kv[j], owned_layer(ss, j), g, upto, true, error, size_of)) return false;
-    if (!kv_validate_sized(image.kv.back(), draft, g, upto, false, error, size_of)) return false;
-    for (size_t i = 0; i < image.stage_parts.size(); ++i) {
-        const ConversationStageSnapshot& part = image.stage_parts[i];
-        const SessionState& sss = *stages.stages[i].session;
-        if (part.layer_lo != sss.layer_lo || part.layer_hi != sss.layer_hi)
-            return fail(error, "layer-split stage part from another session layer range");
-        if (!part.state.imgs.empty() || !part.state.stage_parts.empty() ||
-            part.state.ids.size() != image.live.ids.size() ||
-            !std::equal(part.state.ids.begin(), part.state.ids.end(), image.live.ids.begin()))
-            return fail(error, "layer-split stage part is not a live token prefix");
-        if (!checkpoint_validate_sized(part.state, sss, g, error, size_of)) return false;
-        if (part.kv.size() != owned_count(sss)) return fail(error, "invalid layer-split stage K/V layer count");
-        for (size_t j = 0; j < part.kv.size(); ++j)
-            if (!kv_validate_sized(part.kv[j], owned_layer(sss, j), g, upto, true, error, size_of)) return false;
+    if (!view_ok(view, ss, stages, g, error) ||
+        !session_part_fits(image.live, image.kv, ss, &draft, g, upto, error, size_of))
+        return false;
+    for (int64_t i = 0; i < n_stages; ++i) {
+        const ConversationStageSnapshot& part = image.stage_parts[(size_t) i];
+        const SessionState& stage = *stages.stages[i].session;
+        if (part.layer_lo != stage.layer_lo || part.layer_hi != stage.layer_hi)
+            return fail(error, "a stage part covers other layers than its stage");
+        const bool whole_branch = part.state.imgs.empty() && part.state.stage_parts.empty() &&
+                                  part.state.ids == image.live.ids;
+        if (!whole_branch) return fail(error, "a stage part's running state is not for the whole live branch");
+        if (!session_part_fits(part.state, part.kv, stage, nullptr, g, upto, error, size_of)) return false;
     }
     return true;
 }

@@ -106,15 +106,16 @@ bool shape_kv(ConversationKv& image, const QsaState& st, const ModelGeometry& g,
 /// A session's running state into checkpoint `c` (whose ids are set): the shape twin of enqueue_checkpoint_save.
 bool shape_running(ConversationCheckpoint& c, const SessionState& ss, const ModelGeometry& g, int device, Side& side,
                    std::string& error) {
-    ConversationStateSizes z;
-    if (!running_targets(ss, g, c.ids.size(), z, error)) return false;
-    add_device(side, &c.gdn, device, flat(ss.gdn_state), 0, z.gdn);
-    if (ss.ple_hist) add_device(side, &c.ple, device, flat(ss.ple_hist), 0, z.ple);
-    for (size_t j = 0; j < owned_count(ss); ++j) {
+    RunningState rs;
+    if (!running_state(ss, g, c.ids.size(), rs, error)) return false;
+    const ConversationStateSizes& per = rs.per;
+    add_device(side, &c.gdn, device, flat(ss.gdn_state), 0, rs.gdn());
+    if (rs.keeps_ple) add_device(side, &c.ple, device, flat(ss.ple_hist), 0, rs.ple());
+    for (size_t j = 0; j < rs.layers; ++j) {
         const QsaState& st = owned_layer(ss, j);
-        add_device(side, &c.tails, device, flat(st.idx_tail), 0, z.tail);
-        add_device(side, &c.dead, device, flat(st.idx_dead), 0, z.dead);
-        add_device(side, &c.block_pos, device, flat(st.idx_block_pos), 0, z.block_pos);
+        add_device(side, &c.tails, device, flat(st.idx_tail), 0, per.tail);
+        add_device(side, &c.dead, device, flat(st.idx_dead), 0, per.dead);
+        add_device(side, &c.block_pos, device, flat(st.idx_block_pos), 0, per.block_pos);
     }
     return true;
 }

@@ -49,9 +49,24 @@ bool device_sync(std::string& error);
 size_t owned_count(const SessionState& ss);
 const QsaState& owned_layer(const SessionState& ss, size_t j);
 int64_t stage_count(const ConversationStageSet& s);
-/// The session can hold a `tokens`-long running state (sizes, pointers, indexer capacity); `z` gets the sizes.
-bool running_targets(const SessionState& ss, const ModelGeometry& g, size_t tokens, ConversationStateSizes& z,
-                     std::string& error);
+/// One session's running state for a branch of a given length: the per-buffer sizes (the GDN rows already
+/// scaled to the session's carve; tail, dead key and block position per owned QSA layer) and what the session owns.
+/// Sizing, validation and saving all read their buffer sizes from this one plan.
+struct RunningState {
+    ConversationStateSizes per;
+    size_t layers = 0;        ///< QSA layers the session owns
+    bool keeps_ple = false;   ///< the session keeps a PLE history
+    size_t gdn() const { return per.gdn; }
+    size_t ple() const { return keeps_ple ? per.ple : 0; }
+    size_t tails() const { return layers * per.tail; }
+    size_t dead() const { return layers * per.dead; }
+    size_t block_pos() const { return layers * per.block_pos; }
+};
+/// The plan of `ss`'s running state for a `tokens`-long branch; refused (error set) when the session cannot hold
+/// one that long: a carve outside the model, too few cells, a missing buffer, no spare indexer row.
+bool running_state(const SessionState& ss, const ModelGeometry& g, size_t tokens, RunningState& rs, std::string& error);
+/// Image start positions strictly increasing and inside [0, tokens).
+bool images_ordered(const std::vector<ConversationImageKey>& images, size_t tokens);
 /// The main session plus the stages tile [0, n_layers) in order.
 bool stages_tile(const ConversationStageSet& stages, const SessionState& main_ss, const ModelGeometry& g,
                  std::string& error);
