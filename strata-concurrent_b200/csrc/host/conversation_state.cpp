@@ -37,7 +37,8 @@ DeviceScope::~DeviceScope() {
 }
 
 bool device_sync(std::string& error) {
-    const cudaError_t e = cudaDeviceSynchronize();
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e == cudaSuccess && strata::kv::transfer_fault(strata::kv::TransferStep::device_sync)) e = cudaErrorUnknown;
     if (e == cudaSuccess) return true;
     (void) cudaGetLastError();
     error = std::string("conversation snapshot synchronize: ") + cudaGetErrorString(e);

@@ -6,12 +6,15 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cstdio>
 #include <mutex>
 #include <unordered_map>
 
 namespace strata::kv {
 namespace {
+
+std::atomic<TransferFaultHook> g_fault_hook{nullptr};
 
 struct Staging {
     uint8_t* ptr = nullptr;
@@ -58,6 +61,13 @@ void pieces_of(strata::core::ConversationBuffer& b, uint64_t from, uint64_t to, 
 }
 
 }  // namespace
+
+void set_transfer_fault_hook(TransferFaultHook hook) { g_fault_hook.store(hook); }
+
+bool transfer_fault(TransferStep step) {
+    const TransferFaultHook hook = g_fault_hook.load();
+    return hook && hook(step);
+}
 
 bool transfer_staging(uint64_t bytes, uint8_t** out, std::string& error, const char* what) {
     return staging_for(bytes, out, error, what);
@@ -107,7 +117,23 @@ void Transfer::host_restore(const strata::core::ConversationBuffer& src, uint64_
     if (to > from) host_back_.push_back(HostBack{&src, from, to, dst});
 }
 
+namespace {
+/// cudaMemcpyAsync through the fault seam.
+cudaError_t copy_async(void* dst, const void* src, size_t n, cudaMemcpyKind kind, cudaStream_t stream) {
+    return transfer_fault(TransferStep::copy) ? cudaErrorInvalidValue : cudaMemcpyAsync(dst, src, n, kind, stream);
+}
+}  // namespace
+
 bool Transfer::run(std::string& error, const char* what) {
+    bool enqueued = false;
+    const bool ok = run_queued(error, what, enqueued);
+    // a failure part way leaves earlier copies in flight: let them finish before the caller frees or reuses the host
+    // memory they read or write (the batch's own result stands; this wait's is of no further use)
+    if (!ok && enqueued) (void) cudaStreamSynchronize(nullptr);
+    return ok;
+}
+
+bool Transfer::run_queued(std::string& error, const char* what, bool& enqueued) {
     const cudaStream_t stream = nullptr;   // the legacy stream: ordered after the caller's earlier device work
     bool saving = true;
     for (size_t i = 0; i < items_.size(); ++i) {
@@ -125,8 +151,8 @@ bool Transfer::run(std::string& error, const char* what) {
     for (const HostBack& h : host_back_) {
         bool ok = true;
         h.src->visit(h.from, h.to - h.from, [&](const uint8_t* p, size_t n, size_t at) {
-            ok = cuda_ok(cudaMemcpyAsync(h.dst + at, p, n, cudaMemcpyDefault, stream), error, what,
-                         "host pool copy");
+            ok = cuda_ok(copy_async(h.dst + at, p, n, cudaMemcpyDefault, stream), error, what, "host pool copy");
+            enqueued = enqueued || ok;
             return ok;
         });
         if (!ok) return false;
@@ -134,7 +160,8 @@ bool Transfer::run(std::string& error, const char* what) {
     for (const HostCopy& h : host_) {
         bool ok = true;
         h.dst->visit(h.from, h.to - h.from, [&](uint8_t* p, size_t n, size_t at) {
-            ok = cuda_ok(cudaMemcpyAsync(p, h.src + at, n, cudaMemcpyDefault, stream), error, what, "host pool copy");
+            ok = cuda_ok(copy_async(p, h.src + at, n, cudaMemcpyDefault, stream), error, what, "host pool copy");
+            enqueued = enqueued || ok;
             return ok;
         });
         if (!ok) return false;
@@ -152,9 +179,10 @@ bool Transfer::run(std::string& error, const char* what) {
     for (const Item* it : direct_items)
         for (const Piece& p : it->pieces) {
             uint8_t* dev = const_cast<uint8_t*>(static_cast<const uint8_t*>(it->dev.base)) + it->from + p.rel;
-            const cudaError_t e = it->save ? cudaMemcpyAsync(p.host, dev, p.bytes, cudaMemcpyDeviceToHost, stream)
-                                           : cudaMemcpyAsync(dev, p.host, p.bytes, cudaMemcpyHostToDevice, stream);
+            const cudaError_t e = it->save ? copy_async(p.host, dev, p.bytes, cudaMemcpyDeviceToHost, stream)
+                                           : copy_async(dev, p.host, p.bytes, cudaMemcpyHostToDevice, stream);
             if (!cuda_ok(e, error, what, "running-state copy")) return false;
+            enqueued = true;
         }
     if (!kernel_items.empty()) {
         uint64_t total = 0;
@@ -206,10 +234,15 @@ bool Transfer::run(std::string& error, const char* what) {
         auto launch = [&]() -> bool {
             for (size_t i = 0; i < segs.size(); i += SKV_COPY_MAX_SEGMENTS) {
                 const int n = (int) std::min<size_t>(SKV_COPY_MAX_SEGMENTS, segs.size() - i);
+                if (transfer_fault(TransferStep::launch)) {
+                    error = std::string(what) + ": copy kernel launch failed (injected)";
+                    return false;
+                }
                 if (skv_copy(segs.data() + i, n, SKV_COPY_AUTO, stream) != SKV_OK) {
                     error = std::string(what) + ": " + skv_last_error();
                     return false;
                 }
+                enqueued = true;
             }
             return true;
         };
@@ -218,9 +251,10 @@ bool Transfer::run(std::string& error, const char* what) {
                 for (const Piece& p : kernel_items[i]->pieces) {
                     uint8_t* stage = staging + off[i] + p.rel;
                     const cudaError_t e =
-                        to_host ? cudaMemcpyAsync(p.host, stage, p.bytes, cudaMemcpyDeviceToHost, stream)
-                                : cudaMemcpyAsync(stage, p.host, p.bytes, cudaMemcpyHostToDevice, stream);
+                        to_host ? copy_async(p.host, stage, p.bytes, cudaMemcpyDeviceToHost, stream)
+                                : copy_async(stage, p.host, p.bytes, cudaMemcpyHostToDevice, stream);
                     if (!cuda_ok(e, error, what, to_host ? "device-to-host copy" : "host-to-device copy")) return false;
+                    enqueued = true;
                 }
             return true;
         };
@@ -231,9 +265,13 @@ bool Transfer::run(std::string& error, const char* what) {
         }
         launched = true;
     }
-    for (auto& fn : after_)
+    for (auto& fn : after_) {
+        enqueued = true;   // the follow-up work may have enqueued before it refused
         if (!fn(error)) return false;
-    if (!cuda_ok(cudaStreamSynchronize(stream), error, what, "synchronize")) return false;
+    }
+    cudaError_t synced = cudaStreamSynchronize(stream);
+    if (synced == cudaSuccess && transfer_fault(TransferStep::stream_sync)) synced = cudaErrorUnknown;
+    if (!cuda_ok(synced, error, what, "synchronize")) return false;
     if (launched) {   // the status word the kernels of this batch reported into
         int dev = -1;
         uint32_t status = 0;

@@ -48,10 +48,12 @@ public:
     size_t items() const { return items_.size(); }
 
     /// Run everything queued (saves and restores may not be mixed in one batch).  On failure `error` names the
-    /// reason; a restore that failed after its first write has left partial state.
+    /// reason; a restore that failed after its first write has left partial state.  Either way nothing the batch
+    /// enqueued is still running when it returns, so the caller may free the host memory at once.
     bool run(std::string& error, const char* what);
 
 private:
+    bool run_queued(std::string& error, const char* what, bool& enqueued);
     struct Piece {
         uint8_t* host;
         uint64_t rel;   // offset inside the item's range
@@ -78,6 +80,17 @@ private:
     std::vector<HostBack> host_back_;
     std::vector<std::function<bool(std::string&)>> after_;
 };
+
+/// The host-side steps of a batch, and the snapshot layer's device synchronisations, in the order a park or a mount
+/// issues them.
+enum class TransferStep { device_sync, copy, launch, stream_sync };
+/// Test seam (fault injection): when a hook is set, every step above asks it first, and `true` fails that step as
+/// if the CUDA runtime had returned an error - a copy or a launch is then not issued; a synchronisation still waits
+/// and then reports the error.  No hook is set unless a test sets one.  Process-wide; set it while no batch runs.
+using TransferFaultHook = bool (*)(TransferStep step);
+void set_transfer_fault_hook(TransferFaultHook hook);
+/// True when the hook (if any) fails this step.
+bool transfer_fault(TransferStep step);
 
 /// Bytes of the per-device staging image currently held (for tests and telemetry).
 uint64_t transfer_staging_bytes(int device);

@@ -27,6 +27,9 @@ ORACLE = os.path.join(ROOT, "oracle")
 CUDA = "/usr/local/cuda"
 
 
+HOST_INTERNALS = os.path.join(PKG, "csrc", "host")   # the library's internal headers (the transfer fault seam)
+
+
 def build(name: str) -> str:
     os.makedirs(BIN, exist_ok=True)
     src = os.path.join(SRC, name + ".cpp")
@@ -35,6 +38,7 @@ def build(name: str) -> str:
             os.path.join(ORACLE, "liboracle.so")]
     if not os.path.exists(out) or any(os.path.getmtime(d) > os.path.getmtime(out) for d in deps):
         subprocess.run(["g++", "-std=c++20", "-O2", "-I", os.path.join(ROOT, "include"), "-I", ORACLE,
+                        "-I", HOST_INTERNALS,
                         "-I", f"{CUDA}/include", "-o", out, src, "-L", PKG, "-lstrata_kv", f"-Wl,-rpath,{PKG}",
                         "-L", ORACLE, "-loracle", f"-Wl,-rpath,{ORACLE}", "-L", f"{CUDA}/lib64", "-lcudart",
                         f"-Wl,-rpath,{CUDA}/lib64"], check=True)
@@ -90,3 +94,15 @@ def test_device_mount_agrees_with_host_mount_for_every_format_and_mode(torch_cud
     print(r.stdout)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
     assert "checks passed" in r.stdout
+
+
+def test_transfer_failures_injected_on_the_host(torch_cuda):
+    """Every host-side step of a park and of a mount (device and stream synchronisations, host copies, copy-kernel
+    launches) failed one at a time through the library's fault seam: the reference's transfer-failure cases
+    (src/core/conversation_validation_test.cpp:171-195, 475-500) against this build's batches (see the program's
+    header).  No GPU fault is involved."""
+    exe = build("transfer_faults_gpu_test")
+    r = subprocess.run([exe], capture_output=True, text=True, timeout=600)
+    print(r.stdout)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
+    assert "transfer_faults_gpu_test:" in r.stdout and "checks passed" in r.stdout
