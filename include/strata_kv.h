@@ -127,17 +127,23 @@ SKV_API int skv_copy(const skv_segment* segs, int n_segs, int engine, void* stre
  * token-path allocations, and a park or mount happens between tokens of a running server), a caller
  * that has given every free byte of HBM to its block pool, and any caller that cannot afford the implicit
  * device-wide synchronisation a first cudaMalloc can cause while other streams are decoding.  skv_copy
- * allocates a small status word on a device's first use; this entry point allocates nothing, ever.
+ * allocates a small status word on a device's first use; this entry point never calls an allocator and never
+ * creates that per-device state (skv_device_initialized stays 0 if nothing else ran).
  *
- * It moves the segments with the vector engine in one copy launch, up to SKV_NOALLOC_MAX_SEGMENTS
- * segments per call (skv_copy takes 64).  Its plan and status word live in one fixed-size device array
- * of the library (about 41 KB per GPU, held until the process exits).  More segments than the maximum
- * is refused with SKV_ERANGE before anything is enqueued.
+ * It moves the segments with the vector engine in one copy launch (the vec_ctas_per_sm of
+ * skv_set_copy_tuning), up to SKV_NOALLOC_MAX_SEGMENTS segments per call (skv_copy takes 64).  Its plan and
+ * status word live in one fixed-size device array of the library (about 41 KB per GPU, held until the process
+ * exits).  More segments than the maximum is refused with SKV_ERANGE before anything is enqueued.
  *   status_out  optional; receives the call's SKV_STATUS_* bits (device or mapped pinned host memory),
  *               written in stream order after the copy.
- * Calls share the array: calls issued on one stream are ordered and safe, calls that overlap on the GPU
- * (other streams of the same device) race on it.  The first call on a device does a one-time set-up
- * (symbol address, SM count); make it before any stream capture. */
+ * The first call on a device does a one-time set-up: it looks up the array's device address and the SM count.
+ * Under CUDA's lazy module loading that lookup may load the library's module onto the device (its code and the
+ * array) and can synchronise the device.  So make one warm-up call per device at initialisation, before the
+ * token path starts and before any stream capture.
+ * Calls share the array.  Calls on one stream from ONE host thread at a time are ordered and safe.  Two host
+ * threads issuing calls on the same stream can interleave their plan-writer and copy launches (call A's copy
+ * may then run on call B's plan), and calls that overlap on the GPU (other streams of the same device) race on
+ * the plan and the status word. */
 #define SKV_NOALLOC_MAX_SEGMENTS 512
 SKV_API int skv_copy_noalloc(const skv_segment* segs, int n_segs, uint32_t* status_out, void* stream);
 
@@ -149,6 +155,10 @@ SKV_API int skv_get_copy_tuning(int* tma_stages, uint32_t* tma_tile_bytes, int* 
 
 /* The device status word of `device` (OR of SKV_STATUS_* since the last clear); synchronises `stream`. */
 SKV_API int skv_query_status(int device, void* stream, uint32_t* out_status);
+/* 1 when the library has set up its per-device state on `device` (the SM count and the status word that
+ * skv_copy, skv_query_status and the park / resume calls create on a device's first use), else 0.  A read only:
+ * it sets nothing up.  No counterpart in the reference. */
+SKV_API int skv_device_initialized(int device);
 SKV_API int skv_clear_status(int device, void* stream);
 
 /* ------------------------------------------------------------------ pinned host arena (park / resume)

@@ -411,6 +411,11 @@ int skv_get_copy_tuning(int* tma_stages, uint32_t* tma_tile_bytes, int* tma_ctas
     return SKV_OK;
 }
 
+int skv_device_initialized(int device) {
+    std::lock_guard<std::mutex> lock(g_ctx_mu);
+    return device >= 0 && (size_t) device < g_ctx.size() && g_ctx[(size_t) device] ? 1 : 0;
+}
+
 int skv_query_status(int device, void* stream, uint32_t* out_status) {
     if (!out_status) return fail(SKV_EINVAL, "skv_query_status: null output");
     DeviceScope on(device);

@@ -634,10 +634,11 @@ int launch_wait(const uint64_t* flag, uint64_t value, uint64_t timeout_ns, uint3
 // order from descriptors passed as kernel parameters, then the copy kernel reads it.
 //
 // Every call shares the array (one instance per device) and it keeps the last call's contents.  Calls
-// issued on ONE stream are ordered and safe; calls that overlap on the GPU (different streams of the same
-// device, or host threads racing on one stream) race on the plan and the status word.  The first call on a
-// device performs the set-up (cudaGetSymbolAddress, the SM count); make that first call before any stream
-// capture.
+// issued on ONE stream from one host thread at a time are ordered and safe; calls that overlap on the GPU
+// (different streams of the same device, or host threads racing on one stream) race on the plan and the status
+// word.  The first call on a device performs the set-up (cudaGetSymbolAddress, which may load the module onto
+// the device under lazy loading, and the SM count); make that first call at initialisation, before the token
+// path and before any stream capture.
 namespace skv {
 namespace {
 
@@ -855,7 +856,7 @@ extern "C" int skv_copy_noalloc(const skv_segment* segs, int n_segs, uint32_t* s
     }
     if (const int rc = flush(true)) return rc;   // also clears the status word when every segment was empty
     if (total_tiles) {
-        const unsigned grid = (unsigned) std::min<uint64_t>(total_tiles, (uint64_t) sms * 4);
+        const unsigned grid = (unsigned) std::min<uint64_t>(total_tiles, (uint64_t) sms * tuning().vec_ctas_per_sm);
         copy_vec_noalloc_kernel<<<grid, kVecThreads, 0, stream>>>(plan, total_tiles);
         const cudaError_t le = cudaGetLastError();
         if (le != cudaSuccess) return cuda_fail(le, "skv_copy_noalloc: copy kernel launch");

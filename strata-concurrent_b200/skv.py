@@ -76,6 +76,7 @@ _SIGNATURES = {
     "skv_get_copy_tuning": ([C.POINTER(C.c_int), C.POINTER(C.c_uint32), C.POINTER(C.c_int), C.POINTER(C.c_int)], C.c_int),
     "skv_query_status": ([C.c_int, C.c_void_p, C.POINTER(C.c_uint32)], C.c_int),
     "skv_clear_status": ([C.c_int, C.c_void_p], C.c_int),
+    "skv_device_initialized": ([C.c_int], C.c_int),
     "skv_host_alloc": ([C.c_uint64, C.POINTER(C.c_void_p)], C.c_int),
     "skv_host_free": ([C.c_void_p], C.c_int),
     "skv_host_register": ([C.c_void_p, C.c_uint64], C.c_int),
