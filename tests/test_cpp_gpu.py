@@ -96,6 +96,19 @@ def test_device_mount_agrees_with_host_mount_for_every_format_and_mode(torch_cud
     assert "checks passed" in r.stdout
 
 
+def test_serve_slot_hand_overs_through_the_reference_serve_swap(torch_cuda):
+    """Row a14, the callers: the reference's serve_swap::run drives park / validate / mount hooks written the way
+    src/program/generate.cpp:4185-4266 and 5913-5940 write them, against this build, over three serve slots
+    (tests/cpp/serve_swap_gpu_test.cpp; built by oracle/Makefile because it needs the reference's header)."""
+    exe = os.path.join(ORACLE, "_ref", "serve_swap_gpu_test")
+    if not os.path.exists(exe):
+        pytest.skip("serve_swap_gpu_test not built (the reference tree was not present at build time)")
+    r = subprocess.run([exe], capture_output=True, text=True, timeout=600)
+    print(r.stdout)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
+    assert "serve_swap_gpu_test:" in r.stdout and "checks passed" in r.stdout
+
+
 def test_transfer_failures_injected_on_the_host(torch_cuda):
     """Every host-side step of a park and of a mount (device and stream synchronisations, host copies, copy-kernel
     launches) failed one at a time through the library's fault seam: the reference's transfer-failure cases
