@@ -6,8 +6,9 @@ Outputs
   ref_payload_T{T}.bin   SR4H payloads written by the reference's conversation_snapshot_save +
                          conversation_wire_encode for a small geometry (SMALL below), seed 7.
   golden.json            for each small payload: its FNV-1a payload hash; for config 1 (the full geometry,
-                         4,096 tokens, seed 1): the payload size and hash plus the FNV-1a of every blob the
-                         reference wrote (per-layer K and V, pooled rows, the running state, the ids).
+                         4,096 tokens, seed 1) and for config 2(a)'s length (32,768 tokens, seed 2): the
+                         payload size and hash plus the FNV-1a of every blob the reference wrote (per-layer K
+                         and V, pooled rows, the running state, the ids).
 
 The synthetic inputs come from oracle/kv_oracle.c's seeded generators, so any machine regenerates the same
 caches; the fixtures pin what the reference makes of them.
@@ -29,6 +30,7 @@ SMALL = dict(n_layers=8, qsa_interval=4, n_head_kv=2, head_dim=64, ssm_state_siz
              ssm_conv_channels=16, idx_key_dim=8)
 SMALL_TOKENS = [1, 5, 257]
 CONFIG1_TOKENS = 4096
+CONFIG2A_TOKENS, CONFIG2A_SEED = 32768, 2
 GEOM_HASH, PACK_HASH = 0x1111222233334444, 0x5555666677778888
 
 
@@ -58,6 +60,11 @@ def main() -> None:
     p = sr4h.Payload(data)
     golden["config1"] = {"tokens": CONFIG1_TOKENS, "seed": 1, "bytes": len(data), "payload_hash": h,
                          "snapshot_bytes": O.ref_snapshot_bytes(O.RefPools(s), s.ids), "blobs": blob_hashes(p)}
+    s = O.make_sequence(g, CONFIG2A_TOKENS, seed=CONFIG2A_SEED)
+    data, h = O.ref_snapshot_encode(O.RefPools(s), s.ids, GEOM_HASH, PACK_HASH)
+    golden["config2a_32k"] = {"tokens": CONFIG2A_TOKENS, "seed": CONFIG2A_SEED, "bytes": len(data), "payload_hash": h,
+                              "blobs": blob_hashes(sr4h.Payload(data))}
+    del s, data
     with open(os.path.join(HERE, "golden.json"), "w") as f:
         json.dump(golden, f, indent=1, sort_keys=True)
     print("wrote", len(SMALL_TOKENS), "payloads and golden.json")

@@ -215,6 +215,40 @@ def test_pool_to_pool_32k_round_trip(torch_cuda, engine):
     assert O.page_checksum(host_a, kg.page_bytes) == O.page_checksum(logical.cpu().numpy(), kg.page_bytes)
 
 
+@pytest.mark.slow
+def test_pool_to_pool_32k_matches_the_reference_blobs(torch_cuda):
+    """Config 2(a) at full size, pinned to the reference: the oracle's 32,768-token sequence (seed 2) placed at
+    seed-random slots of a 4,096-block pool, handed pool -> pool into an independent random table of a second pool
+    (ONE TMA-engine launch), then packed out of the DESTINATION through its table: every layer's K and V, the GDN
+    rows and the ids hash (FNV-1a) to what the reference's own conversation_snapshot_save wrote for the same
+    sequence (tests/golden/golden.json config2a_32k), and the destination's unowned slots keep their canary."""
+    torch = torch_cuda
+    golden = json.load(open(GOLDEN))["config2a_32k"]
+    t = golden["tokens"]
+    layers = G_FULL.n_qsa + 1   # the draft layer too, as the reference saves it
+    seq = O.make_sequence(G_FULL, t, seed=golden["seed"])
+    src = Placed(torch, G_FULL, seq, 4096, seed=31, layers=layers)
+    dst = Placed(torch, G_FULL, seq, 4096, seed=47, layers=layers, canary=0x3C, upload=False)
+    kg = src.kg
+    segs = skv.kv_segments_pool_to_pool(src.ps, dst.ps) + skv.state_segments(src.ps, dst.dev_gdn, dst.dev_ids)
+    assert run(torch, segs, skv.COPY_TMA) == 0
+    del src
+    off = skv.image_offsets(kg, t, layers)
+    image = torch.zeros(off["total"], dtype=torch.uint8, device="cuda")
+    assert run(torch, skv.pack_segments(dst.ps, image), skv.COPY_TMA) == 0
+    img = to_host(image)
+    n = kg.pages(t) * kg.page_bytes
+    for j in range(layers):
+        assert [n, O.fnv1a64(image_blob(img, off, (j, 0), n))] == golden["blobs"]["kv"][j]["k"]
+        assert [n, O.fnv1a64(image_blob(img, off, (j, 1), n))] == golden["blobs"]["kv"][j]["v"]
+    assert [kg.gdn_bytes, O.fnv1a64(image_blob(img, off, "gdn", kg.gdn_bytes))] == golden["blobs"]["live"]["gdn"]
+    assert O.fnv1a64(image_blob(img, off, "ids", 4 * t)) == golden["blobs"]["live"]["ids"]
+    owned = np.zeros(4096, dtype=bool)
+    owned[dst.blocks.reshape(-1)] = True
+    pool = to_host(dst.dev_pool).reshape(4096, -1)
+    assert (pool[~owned] == 0x3C).all()
+
+
 @pytest.mark.parametrize("mode", [skv.PARK_DIRECT, skv.PARK_STAGED])
 def test_park_resume_pinned_host(torch_cuda, mode):
     """Config 2b: park to pinned host memory, resume into a different table; both ends bit-exact."""

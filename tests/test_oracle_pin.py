@@ -114,6 +114,24 @@ def test_config1_blob_hashes():
     assert O.metric_bytes(g, c["tokens"]) == 179716096
 
 
+@pytest.mark.slow
+def test_config2a_32k_blob_hashes():
+    """Config 2(a)'s length at full geometry (32,768 tokens, seed 2): the K/V of every layer, the GDN rows and the
+    ids the reference saved, re-derived from the oracle.  The GPU test of the full-size pool->pool hand-off checks
+    its destination against the same reference-written hashes."""
+    c = G["config2a_32k"]
+    g = O.Geometry()
+    s = O.make_sequence(g, c["tokens"], seed=c["seed"])
+    pages = O.pages_for(c["tokens"])
+    assert len(c["blobs"]["kv"]) == g.n_qsa + 1
+    for j, rec in enumerate(c["blobs"]["kv"]):
+        assert rec["k"] == [pages * g.page_bytes, O.fnv1a64(s.k[j])]
+        assert rec["v"] == [pages * g.page_bytes, O.fnv1a64(s.v[j])]
+    assert c["blobs"]["live"]["gdn"] == [g.gdn_bytes, O.fnv1a64(s.gdn)]
+    assert c["blobs"]["live"]["ids"] == O.fnv1a64(s.ids.tobytes())
+    assert O.metric_bytes(g, c["tokens"]) == 884_473_856
+
+
 def test_f16_rounding_is_nearest_even():
     lib = O.lib()
     assert lib.orc_f32_to_f16(1.0) == 0x3C00
