@@ -1,4 +1,5 @@
-// tests/cpp/integration_snippets_cpu_test.cpp - the code INTEGRATION.md shows a maintainer, as functions over the
+// tests/cpp/integration_snippets_cpu_test.cpp - the calls a maintainer adds to the reference engine to bind this
+// library (park_current, the mount hook, the split-role publish and mount), written as functions over the
 // engine's own objects, so that a change of a header that breaks a documented call breaks this build.  Compiled
 // (syntax and types, warnings as errors) by tests/test_cpp_cpu.py; nothing here is run.
 #include "strata_kv.h"

@@ -131,7 +131,8 @@ def test_one_arena_shared_by_threads_has_no_data_race():
 
 
 def test_the_documented_integration_calls_compile():
-    """tests/cpp/integration_snippets_cpu_test.cpp holds the calls INTEGRATION.md shows, over the engine's types."""
+    """tests/cpp/integration_snippets_cpu_test.cpp holds the calls that bind this library into the reference
+    engine, written over the engine's types: they must keep compiling against the headers."""
     r = subprocess.run(["g++", "-std=c++20", "-Wall", "-Wextra", "-Werror", "-fsyntax-only", "-I",
                         os.path.join(ROOT, "include"), "-I", f"{CUDA}/include",
                         os.path.join(SRC, "integration_snippets_cpu_test.cpp")], capture_output=True, text=True,
