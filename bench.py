@@ -1516,9 +1516,8 @@ def run_mixed(args, torch) -> dict | None:
             landed += [h0.elapsed_time(b) for a, b in ev]
             if phased and runs:      # the share of the window this GPU spent waiting for hand-overs
                 idle.append(h0.elapsed_time(h1) - sum(a.elapsed_time(b) for a, b in rev))
-                if args.timeline:
-                    timeline = [[round(h0.elapsed_time(a), 3), round(h0.elapsed_time(b), 3), r["hi"] - r["lo"],
-                                 r["src"], r["phase"], r["wait"] is not None] for r, (a, b) in zip(runs, rev)]
+                timeline = [[round(h0.elapsed_time(a), 3), round(h0.elapsed_time(b), 3), r["hi"] - r["lo"],
+                             r["src"], r["phase"], r["wait"] is not None] for r, (a, b) in zip(runs, rev)]
     skv.set_copy_tuning(*tuning)
     status = torch.tensor([float(skv.query_status(local) != 0)], device="cuda")
     dist.all_reduce(status, op=dist.ReduceOp.MAX)
@@ -1588,6 +1587,7 @@ def run_mixed(args, torch) -> dict | None:
                        "order": args.mixed_order,
                        "parallelism": f"{world // 2} prefill + {world // 2} decode"},
             **({"timeline": {f["rank"]: f["timeline"] for f in dec}} if args.timeline else {}),
+            **({"phases": phase_summary([f["timeline"] for f in dec])} if args.mixed_order == "phased" else {}),
             "handoffs": {"per_decode_gpu_gbs": per_decode, "idle_ms_per_decode_gpu": [f["idle_ms"] for f in dec],
                          "landed_p50_ms": round(float(np.percentile(landed_all, 50)), 4),
                          "landed_p99_ms": round(float(np.percentile(landed_all, 99)), 4),
@@ -1609,6 +1609,26 @@ def run_mixed(args, torch) -> dict | None:
             "port_bound": dict(bound, frac=round(value / bound["gbs"], 4),
                                note="the busiest NVLink port's bytes (a prefill GPU's egress or a decode GPU's "
                                     "ingress) at the measured peer-copy rate: no order of the pulls ends sooner")}
+
+
+def phase_summary(timelines: list) -> list:
+    """Per phase of the port-exclusive order, from the last timed step's runs on every decode GPU (each run
+    [start_ms, end_ms, bytes, source, phase, waited], times from that GPU's step start): the phase's bytes, its
+    span (earliest start to latest end over the GPUs), the aggregate rate over the span, and its slowest run's
+    rate - which phase or boundary limits the step."""
+    by_phase = {}
+    for runs in timelines:
+        for start, end, nbytes, _src, phase, _waited in runs:
+            by_phase.setdefault(phase, []).append((start, end, nbytes))
+    out = []
+    for phase in sorted(by_phase):
+        runs = by_phase[phase]
+        span = max(e for _, e, _ in runs) - min(a for a, _, _ in runs)
+        nbytes = sum(n for _, _, n in runs)
+        slowest = min(n / max(e - a, 1e-6) / 1e6 for a, e, n in runs)
+        out.append({"phase": phase, "runs": len(runs), "bytes": nbytes, "span_ms": round(span, 3),
+                    "gbs": round(nbytes / max(span, 1e-6) / 1e6, 1), "slowest_run_gbs": round(slowest, 1)})
+    return out
 
 
 def pack_image(torch, ps: skv.PooledSequence):

@@ -276,3 +276,15 @@ def test_phase_runs_refuse_segments_that_disagree_with_the_sizes():
     segs = _fake_sequence_segments(kg, i, plan["lengths"][i])[:-1]      # the ids segment left out
     with pytest.raises(ValueError):
         bench.phase_runs(1, plan, sizes, {i: segs}, 4)
+
+
+def test_phase_summary_spans_and_rates():
+    """Config 5's per-phase record: bytes summed over the decode GPUs, the span from the earliest start to the
+    latest end, the aggregate rate over it, and the slowest run's own rate."""
+    tl = [[[0.0, 1.0, 770_000_000, 0, 0, False], [1.1, 2.0, 700_000_000, 2, 1, True]],
+          [[0.05, 1.05, 760_000_000, 2, 0, False], [1.2, 1.9, 100_000_000, 0, 1, True]]]
+    p0, p1 = bench.phase_summary(tl)
+    assert (p0["phase"], p0["runs"], p0["bytes"], p0["span_ms"]) == (0, 2, 1_530_000_000, 1.05)
+    assert p0["gbs"] == pytest.approx(1_530_000_000 / 1.05e-3 / 1e9, abs=0.1)
+    assert p0["slowest_run_gbs"] == pytest.approx(760.0)
+    assert p1["span_ms"] == pytest.approx(0.9) and p1["slowest_run_gbs"] == pytest.approx(100_000_000 / 0.7e-3 / 1e9, abs=0.1)
