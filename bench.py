@@ -63,9 +63,10 @@ def parse():
                          "mixed = N/2 prefill + N/2 decode GPUs, 64 log-uniform sequences, host parks (config 5); "
                          "auto = pairs, plus config 4 at N = 4 and config 5 at N = 8 embedded in the same line")
     ap.add_argument("--chunk-mb", type=int, default=32, help="fan-out chain: pipeline chunk size")
-    ap.add_argument("--mixed-order", default="phased", choices=["phased", "per-source", "serial"],
+    ap.add_argument("--mixed-order", default="phased", choices=["phased", "phased-unfused", "per-source", "serial"],
                     help="config 5: a decode GPU pulls on one stream per source prefill GPU, or one sequence at a "
-                         "time, or in port-exclusive phases (phased_schedule)")
+                         "time, or in port-exclusive phases (phased_schedule; back-to-back runs from one source "
+                         "fused into one launch unless phased-unfused)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--timeline", action="store_true",
@@ -1381,7 +1382,9 @@ def run_mixed(args, torch) -> dict | None:
     multicast) straight into its own pool, in one of three orders (--mixed-order):
 
       phased      (default) port-exclusive phases from phased_schedule: one stream, each prefill GPU read by one
-                  decode GPU at a time, hand-overs by device flags (skv_signal / skv_wait_flag);
+                  decode GPU at a time, hand-overs by device flags (skv_signal / skv_wait_flag); back-to-back runs
+                  from one source with no hand-over between them are one launch (handoff_schedule.fuse_runs;
+                  phased-unfused keeps every run a launch of its own);
       per-source  one stream per source prefill GPU, one skv_copy per sequence, all sources at once;
       serial      one skv_copy per sequence, back to back.
 
@@ -1404,7 +1407,7 @@ def run_mixed(args, torch) -> dict | None:
     held = SeqSet(torch, kg, [lengths[i] for i in (mine_in if decode else mine_out)], args.seed + 7 * rank,
                   fill=not decode)
     slots = SeqSet(torch, kg, [SLOT_TOKENS] * (2 * SERVE_SLOTS), args.seed + 7 * rank + 3, fill=True) if decode else None
-    phased = args.mixed_order == "phased"
+    phased = args.mixed_order in ("phased", "phased-unfused")
     flags = None
     if decode and phased:            # one 8-byte word per run of this GPU's phased order (phased_schedule)
         flags = skv.Pool(local, 1, 4096)
@@ -1439,7 +1442,10 @@ def run_mixed(args, torch) -> dict | None:
     if decode and phased:
         stream_bytes = lambda t: (2 * kg.n_qsa * kg.pages(t) * kg.page_bytes + kg.gdn_bytes  # noqa: E731
                                   + 16 * ((4 * t + 15) // 16))
-        for run in phase_runs(rank, plan, [stream_bytes(t) for t in lengths], segs_of, world):
+        order = phase_runs(rank, plan, [stream_bytes(t) for t in lengths], segs_of, world)
+        if args.mixed_order == "phased":
+            order = handoff_schedule.fuse_runs(order)
+        for run in order:
             pieces = run["pieces"]
             arrays = [((skv.Segment * len(pieces[a:a + skv.MAX_SEGMENTS]))(*pieces[a:a + skv.MAX_SEGMENTS]),
                        len(pieces[a:a + skv.MAX_SEGMENTS])) for a in range(0, len(pieces), skv.MAX_SEGMENTS)]
@@ -1587,7 +1593,7 @@ def run_mixed(args, torch) -> dict | None:
                        "order": args.mixed_order,
                        "parallelism": f"{world // 2} prefill + {world // 2} decode"},
             **({"timeline": {f["rank"]: f["timeline"] for f in dec}} if args.timeline else {}),
-            **({"phases": phase_summary([f["timeline"] for f in dec])} if args.mixed_order == "phased" else {}),
+            **({"phases": phase_summary([f["timeline"] for f in dec])} if phased else {}),
             "handoffs": {"per_decode_gpu_gbs": per_decode, "idle_ms_per_decode_gpu": [f["idle_ms"] for f in dec],
                          "landed_p50_ms": round(float(np.percentile(landed_all, 50)), 4),
                          "landed_p99_ms": round(float(np.percentile(landed_all, 99)), 4),

@@ -87,6 +87,27 @@ def launch_list(sched: dict, destination, flows: dict) -> list:
     return out
 
 
+def fuse_runs(runs: list) -> list:
+    """Merge back-to-back runs of one destination that read the same source with no hand-over between them (the
+    first releases no flag, the second waits for none): one launch then moves both, and the boundary's drain and
+    ramp go.  The fused run keeps the first run's phase and wait and the last one's signal; its pieces, starts and
+    ends are the runs' in order; `fused` counts the runs it replaced."""
+    out = []
+    for run in runs:
+        prev = out[-1] if out else None
+        if prev is not None and prev["src"] == run["src"] and prev["signal"] is None and run["wait"] is None \
+                and prev["hi"] == run["lo"]:
+            prev["hi"] = run["hi"]
+            prev["signal"] = run["signal"]
+            prev["pieces"] = prev["pieces"] + run["pieces"]
+            prev["starts"] = prev["starts"] + run["starts"]
+            prev["ends"] = prev["ends"] + run["ends"]
+            prev["fused"] = prev.get("fused", 1) + 1
+            continue
+        out.append(dict(run))
+    return out
+
+
 def port_bound(demand: dict, rate_gbs: float) -> dict:
     """The schedule-independent bound: the busiest port's bytes at `rate_gbs`."""
     rows, cols = {}, {}

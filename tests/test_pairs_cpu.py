@@ -11,6 +11,7 @@ import torch.distributed as dist
 import torch.multiprocessing as mp
 
 import bench
+import handoff_schedule
 import sched_restatement
 import skv
 
@@ -288,3 +289,34 @@ def test_phase_summary_spans_and_rates():
     assert p0["gbs"] == pytest.approx(1_530_000_000 / 1.05e-3 / 1e9, abs=0.1)
     assert p0["slowest_run_gbs"] == pytest.approx(760.0)
     assert p1["span_ms"] == pytest.approx(0.9) and p1["slowest_run_gbs"] == pytest.approx(100_000_000 / 0.7e-3 / 1e9, abs=0.1)
+
+
+@pytest.mark.parametrize("world,seed", [(8, 1), (8, 5), (8, 9), (4, 2)])
+def test_fused_runs_move_the_same_bytes_with_the_same_hand_overs(world, seed):
+    """Fusing back-to-back runs from one source (no flag between them) changes only the number of launches: each
+    flow's pieces are the same in the same order, every wait and every signal survives exactly once, and no two
+    neighbouring fused runs could be fused further."""
+    kg = skv.KvGeometry()
+    plan = bench.mixed_plan(world, seed)
+    sizes = [2 * kg.n_qsa * kg.pages(t) * kg.page_bytes + kg.gdn_bytes + 16 * ((4 * t + 15) // 16)
+             for t in plan["lengths"]]
+    fused_any = False
+    for d in range(1, world, 2):
+        mine = [i for i in range(len(sizes)) if plan["target"][i] == d]
+        segs_of = {i: _fake_sequence_segments(kg, i, plan["lengths"][i]) for i in mine}
+        runs = bench.phase_runs(d, plan, sizes, segs_of, world)
+        fused = handoff_schedule.fuse_runs(runs)
+        fused_any = fused_any or len(fused) < len(runs)
+        for s in range(0, world, 2):
+            want = _merged([seg for r in runs if r["src"] == s for seg in r["pieces"]])
+            got = _merged([seg for r in fused if r["src"] == s for seg in r["pieces"]])
+            assert got == want
+        assert sorted(r["wait"] for r in fused if r["wait"] is not None) == \
+            sorted(r["wait"] for r in runs if r["wait"] is not None)
+        assert sorted(r["signal"] for r in fused if r["signal"] is not None) == \
+            sorted(r["signal"] for r in runs if r["signal"] is not None)
+        assert sorted(i for r in fused for i in r["starts"]) == sorted(i for r in runs for i in r["starts"])
+        assert sum(r.get("fused", 1) for r in fused) == len(runs)
+        for a, b in zip(fused, fused[1:]):
+            assert not (a["src"] == b["src"] and a["signal"] is None and b["wait"] is None)
+    assert fused_any or world == 4
