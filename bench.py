@@ -68,6 +68,8 @@ def parse():
                          "time, or in port-exclusive phases (phased_schedule; back-to-back runs from one source "
                          "fused into one launch unless phased-unfused)")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-length-sweep", action="store_true",
+                    help="N = 1: leave out the 1K / 4K / 128K pool->pool lines the headline line carries")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--timeline", action="store_true",
                     help="config 5, phased order: add every decode GPU's per-run timeline of the last timed step "
@@ -590,6 +592,9 @@ def run_single(args, torch) -> None:
                          "traffic": traffic_for(kernel, workload), "kernel": kernel,
                          "algorithmic_bytes_per_launch": 2 * b}}
     line["clocks"] = clk.summary()
+    if not args.no_length_sweep:
+        line["length_sweep"] = [pool_to_pool_length(args, torch, kg, n, engine, hbm)
+                                for n in SWEEP_TOKENS if n != t]
     if not args.no_e2e:
         e2e = e2e_park_resume(torch, kg, src, dst, args.steps, max(3, args.warmup), max(3, args.steps // 4))
         pcie = pcie_probe(torch)
@@ -600,6 +605,35 @@ def run_single(args, torch) -> None:
     if not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(t)
     print(json.dumps(line))
+
+
+def pool_to_pool_length(args, torch, kg, t: int, engine: int, hbm: float) -> dict:
+    """Config 2(a)'s operation at another length of config 3's sweep: two fresh pools, min(K, 50) timed steps after
+    the warm-up, CUDA events per step, parity, and the kernel's fraction of the HBM copy peak (2 B(T) per step)."""
+    n_blocks = max(args.pool_blocks, kg.n_qsa * kg.blocks(t))
+    src = SeqOnGpu(torch, kg, t, n_blocks, seed=args.seed + t, fill=True)
+    dst = SeqOnGpu(torch, kg, t, n_blocks, seed=args.seed + t + 1000, fill=False)
+    segs = skv.kv_segments_pool_to_pool(src.ps, dst.ps) + skv.state_segments(src.ps, dst.gdn, dst.ids)
+    arr = (skv.Segment * len(segs))(*segs)
+    stream = torch.cuda.current_stream()
+    L = skv.lib()
+    steps = min(args.steps, 50)
+
+    def step():
+        skv.check(L.skv_copy(arr, len(segs), engine, stream.cuda_stream))
+
+    skv.clear_status(0)
+    total, per = time_steps(torch, stream, step, steps, max(3, args.warmup))
+    parity = (skv.query_status(0) == 0 and bool(torch.equal(dst.logical(torch), src.logical(torch)))
+              and bool(torch.equal(dst.gdn, src.gdn)) and bool(torch.equal(dst.ids, src.ids)))
+    b = kg.metric_bytes(t)
+    p50, p99 = percentiles(per)
+    achieved = 2 * b / (total / steps / 1e3) / 1e9
+    del src, dst
+    torch.cuda.empty_cache()
+    return {"tokens": t, "bytes": b, "steps": steps, "value": round(b * steps / (total / 1e3) / 1e9, 3),
+            "ms_per_step": round(total / steps, 4), "p50_ms": round(p50, 4), "p99_ms": round(p99, 4),
+            "hbm_frac": round(achieved / hbm, 4), "parity": parity}
 
 
 def run_p2p_local(args, torch) -> None:
