@@ -67,6 +67,9 @@ def parse():
                     help="config 5: a decode GPU pulls on one stream per source prefill GPU, or one sequence at a "
                          "time, or in port-exclusive phases (phased_schedule; back-to-back runs from one source "
                          "fused into one launch unless phased-unfused)")
+    ap.add_argument("--tuning", default=None,
+                    help="copy-engine geometry for this run, STAGES,TILE_BYTES,TMA_CTAS_PER_SM[,VEC_CTAS_PER_SM] "
+                         "(skv_set_copy_tuning); default: the library's")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-length-sweep", action="store_true",
                     help="N = 1: leave out the 1K / 4K / 128K pool->pool lines the headline line carries")
@@ -670,7 +673,9 @@ def run_p2p_local(args, torch) -> None:
     print(json.dumps({"scenario": "p2p-local", "metric": METRIC, "value": round(b * args.steps / (total / 1e3) / 1e9, 3),
                       "unit": UNIT, "tokens": t, "bytes_per_step": b, "steps": args.steps, "warmup": args.warmup,
                       "ms_per_step": round(total / args.steps, 4), "p50_ms": round(p50, 4), "p99_ms": round(p99, 4),
-                      "parity": parity, "kernel": "copy_tma_kernel on cuda:1 loading cuda:0's pool"}))
+                      "parity": parity, "kernel": "copy_tma_kernel on cuda:1 loading cuda:0's pool",
+                      "tuning": dict(zip(("tma_stages", "tma_tile_bytes", "tma_ctas_per_sm", "vec_ctas_per_sm"),
+                                         skv.get_copy_tuning()))}))
 
 
 # ------------------------------------------------------------------------------------------------ N > 1: pairs
@@ -1696,11 +1701,23 @@ def brief(line: dict | None, keys=("value", "ms_per_step", "p50_ms", "p99_ms", "
     return out
 
 
+def apply_tuning(spec: str | None) -> None:
+    """--tuning: set the copy-engine geometry for the whole run (the line's config records it)."""
+    if not spec:
+        return
+    parts = [int(x) for x in spec.split(",")]
+    cur = skv.get_copy_tuning()
+    stages, tile, ctas = parts[:3]
+    vec = parts[3] if len(parts) > 3 else cur[3]
+    skv.set_copy_tuning(stages, tile, ctas, vec)
+
+
 def main() -> None:
     args = parse()
     if args.impl == "reference":
         run_reference(args)
         return
+    apply_tuning(args.tuning)
     import torch
     world = int(os.environ.get("WORLD_SIZE", "1"))
     if world == 1 and args.scenario == "p2p-local":
