@@ -986,7 +986,7 @@ def run_pairs(args, torch, tokens: int | None = None, steps: int | None = None, 
                            "tokens": t, "pairs": pairs, "p2p": args.p2p, "bytes_per_step_per_pair": kg.metric_bytes(t),
                            "l2": "inputs larger than L2", "parallelism": f"{pairs} prefill/decode pairs"},
                 "parity": all(ok) and red[1].item() == 0, "parity_by_pair": ok,
-                "gpu_launches": n_steps * (4 if pull else 3) * pairs,
+                "gpu_launches": n_steps * (5 if pull else 3) * pairs,   # pull: wait+copy+signal, signal+wait
                 "roofline": {"bound": "nvlink", "achieved": round(res["per_pair_gbs"], 1), "peak": ref,
                              "unit": "GB/s", "frac": round(res["per_pair_gbs"] / ref, 4),
                              "frac_of_nominal_900": round(res["per_pair_gbs"] / 900.0, 4),
