@@ -55,8 +55,9 @@ def parse():
     ap.add_argument("--engine", default="tma", choices=["tma", "vec"])
     ap.add_argument("--seed", type=int, default=1)
     ap.add_argument("--pool-blocks", type=int, default=4096, help="slots per pool (the configs use 4,096)")
-    ap.add_argument("--p2p", default="pull", choices=["pull", "push", "push-tma"],
-                    help="N > 1: the decode GPU pulls (TMA loads of peer memory), or the prefill GPU pushes (vector "
+    ap.add_argument("--p2p", default="pull", choices=["pull", "pull-gated", "push", "push-tma"],
+                    help="N > 1: the decode GPU pulls (TMA loads of peer memory; pull-gated: the READY wait and the "
+                         "DONE release inside the copy launch, skv_copy_gated), or the prefill GPU pushes (vector "
                          "engine remote stores, or TMA bulk stores to peer memory)")
     ap.add_argument("--scenario", default="auto", choices=["auto", "pairs", "fanout", "mixed", "p2p-local"],
                     help="N > 1: pairs = N/2 prefill->decode pairs; fanout = one prefill to N-1 decodes (config 4); "
@@ -891,7 +892,8 @@ def run_pairs(args, torch, tokens: int | None = None, steps: int | None = None, 
     sp = stream.cuda_stream
     L = skv.lib()
     n_blocks = max(args.pool_blocks, kg.n_qsa * kg.blocks(t))
-    pull = args.p2p == "pull"
+    pull = args.p2p in ("pull", "pull-gated")
+    gated = args.p2p == "pull-gated"
     push_engine = skv.COPY_TMA if args.p2p == "push-tma" else skv.COPY_VEC
     seq = None
     mine = None
@@ -916,7 +918,15 @@ def run_pairs(args, torch, tokens: int | None = None, steps: int | None = None, 
         peer_seq = skv.PooledSequence(kg, skv.Pool(local, n_blocks, kg.block_bytes, memory=peer_pool), t, kg.n_qsa,
                                       None, peer_tables, peer_state, peer_state + lay["ids"])
         counter = [0]
-        if pull and role == "decode":
+        if gated and role == "decode":
+            segs = skv.kv_segments_pool_to_pool(peer_seq, seq.ps) + skv.state_segments(peer_seq, seq.gdn, seq.ids)
+            arr = (skv.Segment * len(segs))(*segs)
+
+            def step():
+                counter[0] += 1   # one launch: wait for READY, pull over NVLink, release DONE on the prefill GPU
+                skv.check(L.skv_copy_gated(arr, len(segs), seq.flag, counter[0], 5_000_000_000, peer_flag, counter[0],
+                                           sp))
+        elif pull and role == "decode":
             segs = skv.kv_segments_pool_to_pool(peer_seq, seq.ps) + skv.state_segments(peer_seq, seq.gdn, seq.ids)
             arr = (skv.Segment * len(segs))(*segs)
 
@@ -986,13 +996,15 @@ def run_pairs(args, torch, tokens: int | None = None, steps: int | None = None, 
                            "tokens": t, "pairs": pairs, "p2p": args.p2p, "bytes_per_step_per_pair": kg.metric_bytes(t),
                            "l2": "inputs larger than L2", "parallelism": f"{pairs} prefill/decode pairs"},
                 "parity": all(ok) and red[1].item() == 0, "parity_by_pair": ok,
-                "gpu_launches": n_steps * (5 if pull else 3) * pairs,   # pull: wait+copy+signal, signal+wait
+                # per pair and step: pull = wait+copy+signal and signal+wait; pull-gated = gated copy and signal+wait;
+                # push = copy+signal and wait
+                "gpu_launches": n_steps * (3 if gated else 5 if pull else 3) * pairs,
                 "roofline": {"bound": "nvlink", "achieved": round(res["per_pair_gbs"], 1), "peak": ref,
                              "unit": "GB/s", "frac": round(res["per_pair_gbs"] / ref, 4),
                              "frac_of_nominal_900": round(res["per_pair_gbs"] / 900.0, 4),
                              "peak_kind": f"peer copy of this run ({'pull' if pull else 'push'} direction, "
                                           "peer_copy_probe); 900 GB/s per direction nominal",
-                             "traffic": None, "kernel": "copy_vec_kernel" if args.p2p == "push" else "copy_tma_kernel"},
+                             "traffic": None, "kernel": {"push": "copy_vec_kernel", "pull-gated": "copy_tma_gated_kernel"}.get(args.p2p, "copy_tma_kernel")},
                 "peer_copy_probe": probe,
                 "clocks": clk.summary()}
         if relay is not None:

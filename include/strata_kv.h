@@ -120,6 +120,18 @@ typedef struct skv_segment {
  * device, peer (P2P over NVLink) or mapped pinned host memory.  n_segs <= SKV_COPY_MAX_SEGMENTS. */
 SKV_API int skv_copy(const skv_segment* segs, int n_segs, int engine, void* stream);
 
+/* skv_copy_gated - skv_copy on the TMA engine with a hand-off's two flags inside the one launch: every CTA
+ * waits until *wait_flag >= wait_value (acquire at system scope, bounded by timeout_ns of device time, 0 = 2 s)
+ * before its first load, and once every CTA has landed all of its tiles the last one stores done_value to
+ * *done_flag with release semantics at system scope, so a GPU or host thread that acquires done_flag reads every
+ * byte.  A wait that runs out sets SKV_STATUS_WAIT_TIMEOUT, that CTA moves nothing and done_flag is not raised.
+ * Either flag may be null; flags are 8-byte aligned device or mapped host words; at least one byte must move.
+ * Replaces skv_wait_flag + skv_copy + skv_signal of a P2P pull (two launches and a flag round trip fewer).  The
+ * gated copies of one device share two counters: issue them from one stream, one after another.  No counterpart in
+ * the reference (it has no P2P path). */
+SKV_API int skv_copy_gated(const skv_segment* segs, int n_segs, const uint64_t* wait_flag, uint64_t wait_value,
+                           uint64_t timeout_ns, uint64_t* done_flag, uint64_t done_value, void* stream);
+
 /* skv_copy_noalloc - the same copy for callers that cannot allocate device memory.
  * No counterpart in the reference (its park path only has synchronous cudaMemcpy calls).
  *

@@ -361,6 +361,34 @@ int skv_copy(const skv_segment* segs, int n_segs, int engine, void* stream) {
     return launch_copy(plan, tiles, engine, *ctx, static_cast<cudaStream_t>(stream));
 }
 
+int skv_copy_gated(const skv_segment* segs, int n_segs, const uint64_t* wait_flag, uint64_t wait_value,
+                   uint64_t timeout_ns, uint64_t* done_flag, uint64_t done_value, void* stream) {
+    DeviceCtx* ctx = current_ctx();
+    if (!ctx) return SKV_ECUDA;
+    if ((reinterpret_cast<uintptr_t>(wait_flag) | reinterpret_cast<uintptr_t>(done_flag)) & 7u)
+        return fail(SKV_EINVAL, "skv_copy_gated: flags must be 8-byte aligned");
+    if (timeout_ns > 60ull * 1000000000ull) return fail(SKV_EINVAL, "skv_copy_gated: timeout must be at most 60 s");
+    CopyPlan plan;
+    uint64_t tiles = 0;
+    if (const int rc = build_plan(segs, n_segs, SKV_COPY_TMA, plan, tiles)) return rc;
+    if (tiles == 0) return fail(SKV_EINVAL, "skv_copy_gated: nothing to move (use skv_wait_flag / skv_signal)");
+    if (!ctx->gate_counters) {
+        cudaError_t e = cudaMalloc(&ctx->gate_counters, 256);
+        if (e == cudaSuccess) e = cudaMemset(ctx->gate_counters, 0, 256);
+        if (e == cudaSuccess) e = cudaDeviceSynchronize();
+        if (e != cudaSuccess) return cuda_fail(e, "skv_copy_gated: counters");
+    }
+    plan.status = ctx->status;
+    GateArgs gate;
+    gate.wait_flag = wait_flag;
+    gate.wait_value = wait_value;
+    gate.timeout_ns = timeout_ns ? timeout_ns : 2000000000ull;
+    gate.done_flag = done_flag;
+    gate.done_value = done_value;
+    gate.counters = ctx->gate_counters;
+    return launch_copy_gated(plan, tiles, gate, *ctx, static_cast<cudaStream_t>(stream));
+}
+
 int skv_copy_chained(const skv_segment* segs, int n_segs, const uint64_t* wait_flags, uint64_t* signal_flags,
                      uint64_t value, uint64_t timeout_ns, void* stream) {
     DeviceCtx* ctx = current_ctx();

@@ -141,6 +141,54 @@ __device__ __forceinline__ LanePage lane_page(const SegDev& sg, uint64_t page, b
     return r;
 }
 
+// ---------------------------------------------------------------- flag waits inside a copy launch
+
+/// Lane 0 reads `flag` once (relaxed, system scope); the whole warp gets `flag >= value`.
+__device__ __forceinline__ bool warp_flag_set(const uint64_t* flag, uint64_t value, int lane) {
+    int ok = 0;
+    if (lane == 0) {
+        uint64_t v;
+        asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(flag) : "memory");
+        ok = v >= value;
+    }
+    return __shfl_sync(0xffffffffu, ok, 0) != 0;
+}
+
+/// Lane 0 polls `flag` >= value for at most timeout_ns with relaxed loads and a growing back-off (every CTA of the
+/// grid may be polling the same word).  Returns the verdict to the whole warp.
+__device__ __forceinline__ bool warp_wait_flag(const uint64_t* flag, uint64_t value, uint64_t timeout_ns, int lane) {
+    int ok = 1;
+    if (lane == 0) {
+        const uint64_t t0 = global_timer_ns();
+        uint32_t pause = 32;
+        for (;;) {
+            uint64_t v;
+            asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(flag) : "memory");
+            if (v >= value) break;
+            if (global_timer_ns() - t0 > timeout_ns) {
+                ok = 0;
+                break;
+            }
+            __nanosleep(pause);
+            pause = min(pause * 2u, 1024u);
+        }
+    }
+    return __shfl_sync(0xffffffffu, ok, 0) != 0;
+}
+
+/// After a flag was seen set: an acquire read of it (lane 0; the flag only grows, so this read sees it set too),
+/// then every lane orders its later bulk (async-proxy) loads after that acquire.
+__device__ __forceinline__ uint64_t ld_acquire_sys(const uint64_t* flag) {
+    uint64_t v;
+    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(flag) : "memory");
+    return v;
+}
+__device__ __forceinline__ void warp_acquire_flag(const uint64_t* flag, int lane) {
+    if (lane == 0) (void) ld_acquire_sys(flag);
+    __syncwarp();
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
 // ---------------------------------------------------------------- TMA bulk engine
 
 /// Per-stage store instructions prepared at load time: lane l issues a bulk store of store_len[l] bytes
@@ -199,7 +247,12 @@ __device__ __forceinline__ void tma_issue_load(const CopyPlan& plan, uint64_t t,
     stash.smem_off[lane] = (uint32_t) lane * (uint32_t) pb;
 }
 
-__global__ void __launch_bounds__(32) copy_tma_kernel(const __grid_constant__ CopyPlan plan, uint64_t total_tiles) {
+/// The TMA engine's work for one CTA: a grid-stride share of the tiles through its ring.  Gated (copy_tma_gated_kernel):
+/// the CTA first waits for the gate's flag (bounded; a wait that runs out moves nothing), and after its last store has
+/// landed it reports to the gate's counters; the last CTA to report raises the done flag if every CTA moved all of
+/// its tiles, then zeroes the counters for the next gated launch in stream order.
+template <bool Gated>
+__device__ __forceinline__ void tma_copy_body(const CopyPlan& plan, uint64_t total_tiles, const GateArgs& gate) {
     extern __shared__ __align__(1024) uint8_t smem[];
     const int stages = plan.tma_stages;
     const uint32_t tile = plan.tma_tile;
@@ -214,7 +267,20 @@ __global__ void __launch_bounds__(32) copy_tma_kernel(const __grid_constant__ Co
     __syncwarp();
 
     const uint64_t first = blockIdx.x, step = gridDim.x;
-    const uint64_t mine = first < total_tiles ? (total_tiles - first + step - 1) / step : 0;
+    uint64_t mine = first < total_tiles ? (total_tiles - first + step - 1) / step : 0;
+    [[maybe_unused]] bool gate_open = true;
+    if constexpr (Gated) {
+        if (gate.wait_flag) {
+            if (warp_flag_set(gate.wait_flag, gate.wait_value, lane) ||
+                warp_wait_flag(gate.wait_flag, gate.wait_value, gate.timeout_ns, lane)) {
+                warp_acquire_flag(gate.wait_flag, lane);
+            } else {
+                if (lane == 0) atomicOr(plan.status, SKV_STATUS_WAIT_TIMEOUT);
+                gate_open = false;
+                mine = 0;
+            }
+        }
+    }
     uint64_t issued = 0;
     for (; issued < mine && issued < (uint64_t) stages; ++issued)
         tma_issue_load(plan, first + issued * step, ring + (issued % stages) * tile, &bars[issued % stages],
@@ -250,6 +316,42 @@ __global__ void __launch_bounds__(32) copy_tma_kernel(const __grid_constant__ Co
             (void) mbar_wait_bounded(&bars[j % stages], (uint32_t) ((j / stages) & 1u));
     }
     bulk_wait_all();
+    if constexpr (Gated) {
+        if (gate.done_flag) {
+            // this CTA's bulk stores have landed (wait_group 0); order them before the generic-proxy report
+            asm volatile("fence.proxy.async.global;" ::: "memory");
+            __syncwarp();
+            if (lane == 0) {
+                if (gate_open && !timed_out)
+                    asm volatile("red.relaxed.gpu.global.add.u32 [%0], 1;" ::"l"(gate.counters + 1) : "memory");
+                uint32_t before;
+                // gpu-scope acq_rel: gathers every CTA's landed stores (and good count) into the last reporter's view
+                asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(before) : "l"(gate.counters) : "memory");
+                if (before + 1 == gridDim.x) {
+                    uint32_t good;
+                    asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(good) : "l"(gate.counters + 1) : "memory");
+                    gate.counters[0] = 0;   // zero for the next gated launch (it starts after this one ends)
+                    gate.counters[1] = 0;
+                    // system-scope release, cumulative over what this thread acquired: a peer GPU that acquires the
+                    // flag reads every byte of the copy
+                    if (good == gridDim.x)
+                        asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(gate.done_flag), "l"(gate.done_value)
+                                     : "memory");
+                }
+            }
+        }
+    }
+}
+
+__global__ void __launch_bounds__(32) copy_tma_kernel(const __grid_constant__ CopyPlan plan, uint64_t total_tiles) {
+    tma_copy_body<false>(plan, total_tiles, GateArgs{});
+}
+
+/// skv_copy_gated: the TMA engine with the hand-off's READY wait before the first load and its DONE release after
+/// the last store, inside the one launch.
+__global__ void __launch_bounds__(32) copy_tma_gated_kernel(const __grid_constant__ CopyPlan plan, uint64_t total_tiles,
+                                                            const __grid_constant__ GateArgs gate) {
+    tma_copy_body<true>(plan, total_tiles, gate);
 }
 
 // ---------------------------------------------------------------- chained TMA engine
@@ -264,52 +366,6 @@ __global__ void __launch_bounds__(32) copy_tma_kernel(const __grid_constant__ Co
 // that completes the count stores value to signal_flags[c] with release semantics at system scope, so a peer
 // GPU that acquires that flag reads every byte of chunk c.  A wait that runs out stops new loads (status
 // WAIT_TIMEOUT); loaded tiles are still stored, and a chunk is signalled only if every one of its tiles landed.
-
-/// Lane 0 reads `flag` once (relaxed, system scope); the whole warp gets `flag >= value`.
-__device__ __forceinline__ bool warp_flag_set(const uint64_t* flag, uint64_t value, int lane) {
-    int ok = 0;
-    if (lane == 0) {
-        uint64_t v;
-        asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(flag) : "memory");
-        ok = v >= value;
-    }
-    return __shfl_sync(0xffffffffu, ok, 0) != 0;
-}
-
-/// Lane 0 polls `flag` >= value for at most timeout_ns with relaxed loads and a growing back-off (every CTA of the
-/// grid may be polling the same word).  Returns the verdict to the whole warp.
-__device__ __forceinline__ bool warp_wait_flag(const uint64_t* flag, uint64_t value, uint64_t timeout_ns, int lane) {
-    int ok = 1;
-    if (lane == 0) {
-        const uint64_t t0 = global_timer_ns();
-        uint32_t pause = 32;
-        for (;;) {
-            uint64_t v;
-            asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(flag) : "memory");
-            if (v >= value) break;
-            if (global_timer_ns() - t0 > timeout_ns) {
-                ok = 0;
-                break;
-            }
-            __nanosleep(pause);
-            pause = min(pause * 2u, 1024u);
-        }
-    }
-    return __shfl_sync(0xffffffffu, ok, 0) != 0;
-}
-
-/// After a flag was seen set: an acquire read of it (lane 0; the flag only grows, so this read sees it set too),
-/// then every lane orders its later bulk (async-proxy) loads after that acquire.
-__device__ __forceinline__ uint64_t ld_acquire_sys(const uint64_t* flag) {
-    uint64_t v;
-    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(flag) : "memory");
-    return v;
-}
-__device__ __forceinline__ void warp_acquire_flag(const uint64_t* flag, int lane) {
-    if (lane == 0) (void) ld_acquire_sys(flag);
-    __syncwarp();
-    asm volatile("fence.proxy.async.global;" ::: "memory");
-}
 
 constexpr uint32_t kChainClaimBatch = 2;   // consecutive tiles per claim: fewer atomics, chunks still land in order
 
@@ -554,6 +610,23 @@ int launch_copy(const CopyPlan& plan, uint64_t total_tiles, int engine, DeviceCt
     }
     const cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? SKV_OK : cuda_fail(e, "copy kernel launch");
+}
+
+int launch_copy_gated(const CopyPlan& plan, uint64_t total_tiles, const GateArgs& gate, DeviceCtx& ctx,
+                      cudaStream_t stream) {
+    if (total_tiles == 0) return fail(SKV_EINVAL, "skv_copy_gated: nothing to move");
+    const Tuning tu = tuning();
+    const size_t smem = tma_smem_bytes(plan.tma_stages, plan.tma_tile);
+    if (ctx.tma_gated_smem_configured < smem) {
+        const cudaError_t e =
+            cudaFuncSetAttribute(copy_tma_gated_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(copy_tma_gated_kernel)");
+        ctx.tma_gated_smem_configured = smem;
+    }
+    const unsigned grid = (unsigned) std::min<uint64_t>(total_tiles, (uint64_t) ctx.sms * tu.tma_ctas_per_sm);
+    copy_tma_gated_kernel<<<grid, 32, smem, stream>>>(plan, total_tiles, gate);
+    const cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? SKV_OK : cuda_fail(e, "gated copy kernel launch");
 }
 
 int launch_copy_chained(const CopyPlan& plan, uint64_t total_tiles, const ChainArgs& chain, DeviceCtx& ctx,

@@ -60,6 +60,16 @@ Tuning tuning();
 /// Dynamic shared memory one TMA CTA needs for `stages` x `tile`.
 size_t tma_smem_bytes(int stages, uint32_t tile);
 
+/// A copy launch gated by flags (skv_copy_gated).
+struct GateArgs {
+    const uint64_t* wait_flag = nullptr;   // every CTA waits for *wait_flag >= wait_value before its first load
+    uint64_t wait_value = 0;
+    uint64_t timeout_ns = 0;
+    uint64_t* done_flag = nullptr;         // the last CTA to land stores done_value here (release, system scope)
+    uint64_t done_value = 0;
+    uint32_t* counters = nullptr;          // [0] CTAs reported, [1] CTAs that moved all their tiles; zero between launches
+};
+
 /// Per-device runtime facts the launchers need (SM count, the status word).
 struct DeviceCtx {
     int device = -1;
@@ -67,6 +77,8 @@ struct DeviceCtx {
     uint32_t* status = nullptr;
     size_t tma_smem_configured = 0;   // the copy_tma_kernel dynamic-smem limit set on this device so far
     size_t tma_chain_smem_configured = 0;
+    size_t tma_gated_smem_configured = 0;
+    uint32_t* gate_counters = nullptr;   // skv_copy_gated's two counters (allocated zeroed on first use)
     uint32_t* chain_landed = nullptr; // skv_copy_chained scratch (kChainScratchBytes, allocated on first use)
 };
 
@@ -97,6 +109,9 @@ int cuda_fail(cudaError_t e, const char* what);
 
 /// Launch one copy kernel for a prepared plan.  `engine` is SKV_COPY_TMA or SKV_COPY_VEC.
 int launch_copy(const CopyPlan& plan, uint64_t total_tiles, int engine, DeviceCtx& ctx, cudaStream_t stream);
+/// Launch the gated TMA kernel (skv_copy_gated).
+int launch_copy_gated(const CopyPlan& plan, uint64_t total_tiles, const GateArgs& gate, DeviceCtx& ctx,
+                      cudaStream_t stream);
 /// Launch the chained TMA kernel (the counters are reset on `stream` first).
 int launch_copy_chained(const CopyPlan& plan, uint64_t total_tiles, const ChainArgs& chain, DeviceCtx& ctx,
                         cudaStream_t stream);

@@ -71,6 +71,8 @@ _SIGNATURES = {
     "skv_expand_block_table": ([C.c_void_p, C.c_int64, C.c_int64, C.c_int64, C.c_int64, C.c_void_p], C.c_int),
     "skv_copy": ([C.c_void_p, C.c_int, C.c_int, C.c_void_p], C.c_int),
     "skv_copy_noalloc": ([C.c_void_p, C.c_int, C.c_void_p, C.c_void_p], C.c_int),
+    "skv_copy_gated": ([C.c_void_p, C.c_int, C.c_void_p, C.c_uint64, C.c_uint64, C.c_void_p, C.c_uint64, C.c_void_p],
+                       C.c_int),
     "skv_copy_chained": ([C.c_void_p, C.c_int, C.c_void_p, C.c_void_p, C.c_uint64, C.c_uint64, C.c_void_p], C.c_int),
     "skv_set_copy_tuning": ([C.c_int, C.c_uint32, C.c_int, C.c_int], C.c_int),
     "skv_get_copy_tuning": ([C.POINTER(C.c_int), C.POINTER(C.c_uint32), C.POINTER(C.c_int), C.POINTER(C.c_int)], C.c_int),
@@ -214,6 +216,15 @@ def copy_chained(segs: list, wait_flags=None, signal_flags=None, value: int = 1,
     arr = (Segment * len(segs))(*segs)
     check(lib().skv_copy_chained(arr, len(segs), _ptr(wait_flags), _ptr(signal_flags), int(value), int(timeout_ns),
                                  _stream(stream)))
+
+
+def copy_gated(segs: list, wait_flag=None, wait_value: int = 0, done_flag=None, done_value: int = 0,
+               timeout_ns: int = 0, stream=None) -> None:
+    """ONE TMA launch moving `segs` that first waits for *wait_flag >= wait_value and, once everything landed,
+    releases done_value into *done_flag (either flag may be None)."""
+    arr = (Segment * len(segs))(*segs)
+    check(lib().skv_copy_gated(arr, len(segs), _ptr(wait_flag), int(wait_value), int(timeout_ns), _ptr(done_flag),
+                               int(done_value), _stream(stream)))
 
 
 def set_copy_tuning(tma_stages: int, tma_tile_bytes: int, tma_ctas_per_sm: int, vec_ctas_per_sm: int) -> None:

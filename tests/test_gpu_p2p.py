@@ -7,7 +7,8 @@ move it, each straight into the destination pool with no intermediate contiguous
   pull       the decode GPU's TMA engine issues bulk loads of the prefill GPU's pool pages (peer memory, no
              multicast) and bulk stores into its own slots;
   push       the prefill GPU's vector engine stores 16-byte words into the decode GPU's slots;
-  push-tma   the prefill GPU's TMA engine bulk-stores into the decode GPU's slots.
+  push-tma   the prefill GPU's TMA engine bulk-stores into the decode GPU's slots;
+  pull-gated the pull as ONE launch (skv_copy_gated): the copy waits for READY and releases DONE itself.
 
 The WHOLE destination pool is compared with the oracle's scatter of the same cache through the destination's
 tables (tests/test_gpu_parity.py's placement), so a stray write into a slot the sequence does not own shows as a
@@ -27,7 +28,7 @@ from test_gpu_parity import G_FULL, G_SMALL, Placed
 pytestmark = pytest.mark.gpu
 
 WAIT_NS = 2_000_000_000   # every flag wait ends by itself after 2 s of device time
-METHODS = [("pull", skv.COPY_TMA), ("push", skv.COPY_VEC), ("push-tma", skv.COPY_TMA)]
+METHODS = [("pull", skv.COPY_TMA), ("push", skv.COPY_VEC), ("push-tma", skv.COPY_TMA), ("pull-gated", skv.COPY_TMA)]
 PREFILL, DECODE = 0, 1
 
 
@@ -51,7 +52,13 @@ def hand_off(torch, src: Placed, dst: Placed, method: str, engine: int, round_no
     torch.cuda.synchronize(DECODE)
     segs = skv.kv_segments_pool_to_pool(src.ps, dst.ps) + skv.state_segments(src.ps, dst.dev_gdn, dst.dev_ids)
     L = skv.lib()
-    if method == "pull":
+    if method == "pull-gated":
+        with torch.cuda.device(DECODE):   # one launch: waits for READY, pulls, releases DONE on the prefill GPU
+            skv.copy_gated(segs, flag_d.data_ptr(), round_no, flag_p.data_ptr(), round_no, timeout_ns=WAIT_NS)
+        with torch.cuda.device(PREFILL):
+            skv.check(L.skv_signal(flag_d.data_ptr(), round_no, None))                         # READY
+            skv.check(L.skv_wait_flag(flag_p.data_ptr(), round_no, WAIT_NS, None))             # DONE
+    elif method == "pull":
         with torch.cuda.device(DECODE):   # enqueue the waiting side first: it waits on the other GPU
             skv.check(L.skv_wait_flag(flag_d.data_ptr(), round_no, WAIT_NS, None))            # READY
             skv.copy(segs, engine)                                                             # loads over NVLink
@@ -68,7 +75,7 @@ def hand_off(torch, src: Placed, dst: Placed, method: str, engine: int, round_no
     torch.cuda.synchronize(PREFILL)
     torch.cuda.synchronize(DECODE)
     assert int(flag_d.item()) == round_no
-    if method == "pull":
+    if method.startswith("pull"):
         assert int(flag_p.item()) == round_no
     return skv.query_status(PREFILL), skv.query_status(DECODE)
 

@@ -351,3 +351,44 @@ def test_flag_wait_times_out_and_signal_releases(torch_cuda):
     skv.check(skv.lib().skv_wait_flag(flag.data_ptr(), 7, 1_000_000_000, None))
     torch.cuda.synchronize()
     assert skv.query_status(0) == 0 and torch.equal(src, dst) and int(flag[0]) == 7
+
+
+def test_gated_copy_waits_releases_and_times_out(torch_cuda):
+    """skv_copy_gated on one GPU.  A gate raised earlier on the same stream opens the copy, which lands exactly the
+    oracle's scatter and then raises its done flag; a gate nobody raises ends after its limit with the timeout bit,
+    nothing moved and no done flag; done-only launches twice in a row each raise their flag (the shared counters
+    start from zero again after every launch, the timed-out one included)."""
+    torch = torch_cuda
+    pb, pages, limit = 4096, 200, 512
+    image = np.random.default_rng(5).integers(0, 256, pages * pb, dtype=np.uint8)
+    table = O.permutation(limit, seed=6)[:pages].copy()
+    expect = np.full(limit * pb, 0x77, dtype=np.uint8)
+    O.scatter_pages(image, table, pages, pb, expect)
+    src = torch.from_numpy(image).cuda()
+    pool = torch.full((limit * pb,), 0x77, dtype=torch.uint8, device="cuda")
+    dt = torch.from_numpy(table).cuda()
+    flags = torch.zeros(4, dtype=torch.int64, device="cuda")
+    f = [flags.data_ptr() + 8 * i for i in range(4)]
+    seg = skv.segment(src, pool, pages * pb, dst_pages=dt, page_bytes=pb, dst_page_limit=limit)
+    skv.clear_status(0)
+    skv.signal(f[0], 3)                                     # the gate, raised before the copy on the same stream
+    skv.copy_gated([seg], f[0], 3, f[1], 9, timeout_ns=1_000_000_000)
+    torch.cuda.synchronize()
+    assert skv.query_status(0) == 0 and int(flags[1]) == 9
+    assert (pool.cpu().numpy() == expect).all()
+
+    pool.fill_(0x77)
+    skv.clear_status(0)
+    skv.copy_gated([seg], f[2], 1, f[3], 5, timeout_ns=2_000_000)   # nobody raises f[2]
+    torch.cuda.synchronize()
+    assert skv.query_status(0) == skv.STATUS_WAIT_TIMEOUT
+    assert int(flags[3]) == 0 and int((pool != 0x77).sum()) == 0
+
+    skv.clear_status(0)
+    for v in (11, 12):
+        skv.copy_gated([seg], None, 0, f[3], v)
+        torch.cuda.synchronize()
+        assert int(flags[3]) == v
+    assert skv.query_status(0) == 0 and (pool.cpu().numpy() == expect).all()
+    with pytest.raises(skv.SkvError, match="nothing to move"):
+        skv.copy_gated([skv.segment(src, pool, 0)], None, 0, f[3], 1)
