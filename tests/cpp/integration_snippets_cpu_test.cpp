@@ -41,6 +41,10 @@ void pull(uint64_t* ready_flag, uint64_t* done_flag, uint64_t seq_no, const skv_
     skv_copy(segs, n, SKV_COPY_TMA, stream);
     skv_signal(done_flag, seq_no, stream);
 }
+void pull_gated(uint64_t* ready_flag, uint64_t* done_flag, uint64_t seq_no, const skv_segment* segs, int n,
+                void* stream) {
+    skv_copy_gated(segs, n, ready_flag, seq_no, 2'000'000'000, done_flag, seq_no, stream);
+}
 
 // 3. one GPU of a pushed chain
 void chain_hop(int k, const skv_segment* chunks, int n_chunks, const uint64_t* my_flags, uint64_t* next_flags,
