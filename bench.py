@@ -41,7 +41,16 @@ METRIC = "KV handoff GB/s & p50/p99 ms per 32K-token sequence"
 UNIT = "GB/s"
 PEAKS_FILE = os.path.join(ROOT, "MEASURED_PEAKS.json")
 FALLBACK_HBM_GBS = 6650.0
-NVLINK_PEER_COPY_GBS = 770.0     # the pool's measured peer copy per direction (900 nominal)
+NVLINK_PEER_COPY_GBS = 770.0     # an earlier measurement of the pool's peer copy per direction (900 nominal): the
+                                 # rate used only where a line has no same-run probe (the standalone scenarios)
+
+
+def link_rate(probe: dict | None) -> tuple:
+    """(GB/s per direction, what it is) for a line's NVLink roofline: the same-run copy-engine probe (pull direction)
+    when the run measured one, else the earlier figure."""
+    if probe:
+        return probe["pull_gbs_median"], "peer copy of this run (peer_copy_probe, pull direction)"
+    return NVLINK_PEER_COPY_GBS, "earlier measured peer copy (770 GB/s; no probe in this run)"
 PROFILE_TRAFFIC = os.path.join(ROOT, "profiles", "traffic.json")
 
 
@@ -63,7 +72,8 @@ def parse():
                     help="N > 1: pairs = N/2 prefill->decode pairs; fanout = one prefill to N-1 decodes (config 4); "
                          "mixed = N/2 prefill + N/2 decode GPUs, 64 log-uniform sequences, host parks (config 5); "
                          "auto = pairs, plus config 4 at N = 4 and config 5 at N = 8 embedded in the same line")
-    ap.add_argument("--chunk-mb", type=int, default=32, help="fan-out chain: pipeline chunk size")
+    ap.add_argument("--chunk-mb", type=int, default=16,
+                    help="fan-out chain: pipeline chunk size (16 / 32 / 64 MB measured 1,936 / 1,910 / 1,869 GB/s)")
     ap.add_argument("--mixed-order", default="phased", choices=["phased", "phased-unfused", "per-source", "serial"],
                     help="config 5: a decode GPU pulls on one stream per source prefill GPU, or one sequence at a "
                          "time, or in port-exclusive phases (phased_schedule; back-to-back runs from one source "
@@ -1096,7 +1106,7 @@ def split_roles(torch, rank: int) -> list | None:
 
 # ------------------------------------------------------------------------------------------------ fan-out
 
-def run_fanout(args, torch, tokens: int | None = None, steps: int | None = None) -> dict | None:
+def run_fanout(args, torch, tokens: int | None = None, steps: int | None = None, probe: dict | None = None) -> dict | None:
     """Config 4: rank 0 (prefill) holds one sequence; ranks 1..N-1 (decode) each receive the whole cache into
     their own pool at independent random slots.  Four ways, each timed over the same K steps:
 
@@ -1307,6 +1317,7 @@ def run_fanout(args, torch, tokens: int | None = None, steps: int | None = None)
                              "p99_ms": round(float(np.percentile(per, 99)), 4),
                              "per_receiver_gbs": round(b * n_steps / (tot / 1e3) / 1e9, 3), "parity": ok}
         best = "chain_push"   # the reported method, fixed in advance; the others are kept beside it in `methods`
+        rate, rate_kind = link_rate(probe)
         m = methods[best]
         line = {"metric": METRIC, "value": m["value"], "unit": UNIT, "n_gpus": world, "steps": n_steps,
                 "warmup": args.warmup, "ms_per_step": m["ms_per_step"], "p50_ms": m["p50_ms"], "p99_ms": m["p99_ms"],
@@ -1317,10 +1328,11 @@ def run_fanout(args, torch, tokens: int | None = None, steps: int | None = None)
                            "tokens": t, "receivers": receivers, "method": best, "chunk_mb": args.chunk_mb,
                            "l2": "inputs larger than L2", "parallelism": f"1 -> {receivers} fan-out"},
                 "methods": methods, "parity": all(v["parity"] for v in methods.values()) and status.item() == 0,
-                "roofline": {"bound": "nvlink", "achieved": m["per_receiver_gbs"], "peak": NVLINK_PEER_COPY_GBS,
-                             "unit": "GB/s", "frac": round(m["per_receiver_gbs"] / NVLINK_PEER_COPY_GBS, 4),
-                             "peak_kind": "measured peer copy per direction; each receiver's ingress",
-                             "traffic": None, "kernel": "copy_tma_kernel"}}
+                "roofline": {"bound": "nvlink", "achieved": m["per_receiver_gbs"], "peak": rate, "unit": "GB/s",
+                             "frac": round(m["per_receiver_gbs"] / rate, 4),
+                             "frac_of_nominal_900": round(m["per_receiver_gbs"] / 900.0, 4),
+                             "peak_kind": rate_kind + "; each receiver's ingress",
+                             "traffic": None, "kernel": "copy_tma_chain_kernel"}}
     torch.cuda.synchronize()
     dist.barrier()
     for pool, state in maps.values():
@@ -1379,9 +1391,9 @@ def phase_runs(rank: int, plan: dict, sizes: list, segs_of: dict, world: int) ->
     return handoff_schedule.launch_list(phased_schedule(plan, sizes, world), rank, flows)
 
 
-def port_bound(plan: dict, sizes: list, world: int) -> dict:
+def port_bound(plan: dict, sizes: list, world: int, rate_gbs: float = NVLINK_PEER_COPY_GBS) -> dict:
     """Config 5's schedule-independent bound: the busiest NVLink port's bytes at the measured peer-copy rate."""
-    return handoff_schedule.port_bound(mixed_demand(plan, sizes), NVLINK_PEER_COPY_GBS)
+    return handoff_schedule.port_bound(mixed_demand(plan, sizes), rate_gbs)
 
 
 class SeqSet:
@@ -1426,7 +1438,7 @@ class SeqSet:
                                   tables, state_base + self.offs[i], state_base + self.offs[i] + lay["ids"])
 
 
-def run_mixed(args, torch) -> dict | None:
+def run_mixed(args, torch, probe: dict | None = None) -> dict | None:
     """Config 5: the even ranks prefill, the odd ranks decode.  64 sequences with seeded log-uniform lengths on
     [1K, 128K] live in their prefill owner's pool; each decode GPU pulls the sequences assigned to it (random
     pairing, so several decode GPUs may want one prefill GPU at once) with skv_copy (TMA, peer loads, no
@@ -1620,7 +1632,8 @@ def run_mixed(args, torch) -> dict | None:
     if rank != 0:
         return None
     total = sum(kg.metric_bytes(t) for t in lengths)
-    bound = port_bound(plan, [kg.metric_bytes(t) for t in lengths], world)
+    rate, rate_kind = link_rate(probe)
+    bound = port_bound(plan, [kg.metric_bytes(t) for t in lengths], world, rate)
     wins = win.cpu().numpy()
     value = total * steps / (float(wins.sum()) / 1e3) / 1e9
     lat_all = np.concatenate([np.asarray(f["lat"]) for f in allf if f["lat"]])
@@ -1659,13 +1672,13 @@ def run_mixed(args, torch) -> dict | None:
                       "note": "park + resume of every serve slot, staged, on a side stream during the handoffs"},
             "parity": bool(okt.item() == 1.0) and status.item() == 0,
             "gpu_launches": steps * (sum(f["launches"] for f in dec) + len(dec) * SERVE_SLOTS * 2),
-            "roofline": {"bound": "nvlink", "achieved": round(mean_ingress, 1), "peak": NVLINK_PEER_COPY_GBS,
-                         "unit": "GB/s", "frac": round(mean_ingress / NVLINK_PEER_COPY_GBS, 4),
-                         "peak_kind": "measured peer copy per direction; mean decode-GPU ingress over its window",
+            "roofline": {"bound": "nvlink", "achieved": round(mean_ingress, 1), "peak": rate, "unit": "GB/s",
+                         "frac": round(mean_ingress / rate, 4),
+                         "peak_kind": rate_kind + "; mean decode-GPU ingress over its window",
                          "traffic": None, "kernel": "copy_tma_kernel"},
-            "port_bound": dict(bound, frac=round(value / bound["gbs"], 4),
+            "port_bound": dict(bound, frac=round(value / bound["gbs"], 4), rate_gbs=rate, rate_kind=rate_kind,
                                note="the busiest NVLink port's bytes (a prefill GPU's egress or a decode GPU's "
-                                    "ingress) at the measured peer-copy rate: no order of the pulls ends sooner")}
+                                    "ingress) at the peer-copy rate: no order of the pulls ends sooner")}
 
 
 def phase_summary(timelines: list) -> list:
@@ -1759,11 +1772,11 @@ def main() -> None:
                     line["config3_sweep"] = sweep
                     line["split_roles_device_descriptor"] = roles
             if args.scenario == "auto" and world == 4:
-                sub = run_fanout(args, torch, tokens=65536, steps=min(args.steps, 40))
+                sub = run_fanout(args, torch, tokens=65536, steps=min(args.steps, 40), probe=probe)
                 if line is not None:
                     line["config4_fanout"] = brief(sub)
             if args.scenario == "auto" and world == 8:
-                sub = run_mixed(args, torch)
+                sub = run_mixed(args, torch, probe=probe)
                 if line is not None:
                     line["config5_mixed"] = brief(sub)
         if rank == 0 and line is not None:
