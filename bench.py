@@ -68,10 +68,11 @@ def parse():
                     help="N > 1: the decode GPU pulls (TMA loads of peer memory; pull-gated: the READY wait and the "
                          "DONE release inside the copy launch, skv_copy_gated), or the prefill GPU pushes (vector "
                          "engine remote stores, or TMA bulk stores to peer memory)")
-    ap.add_argument("--scenario", default="auto", choices=["auto", "pairs", "fanout", "mixed", "p2p-local"],
+    ap.add_argument("--scenario", default="auto", choices=["auto", "pairs", "sweep", "fanout", "mixed", "p2p-local"],
                     help="N > 1: pairs = N/2 prefill->decode pairs; fanout = one prefill to N-1 decodes (config 4); "
                          "mixed = N/2 prefill + N/2 decode GPUs, 64 log-uniform sequences, host parks (config 5); "
-                         "auto = pairs, plus config 4 at N = 4 and config 5 at N = 8 embedded in the same line")
+                         "auto = pairs, plus config 3's sweep and the split-role record at N = 2, config 4 at N = 4 "
+                         "and config 5 at N = 8 embedded in the same line; sweep = pairs and config 3's sweep only")
     ap.add_argument("--chunk-mb", type=int, default=16,
                     help="fan-out chain: pipeline chunk size (16 / 32 / 64 MB measured 1,936 / 1,910 / 1,869 GB/s)")
     ap.add_argument("--mixed-order", default="phased", choices=["phased", "phased-unfused", "per-source", "serial"],
@@ -1765,11 +1766,13 @@ def main() -> None:
             # the headline: N/2 pairs (configs 3/5 throughput, weak scaling); at N = 4 and N = 8 the same run also
             # measures BASELINE's own 4- and 8-GPU configs and embeds them
             line, probe = run_pairs(args, torch)
-            if args.scenario == "auto" and world == 2:
+            if args.scenario in ("auto", "sweep") and world == 2:
                 sweep = pair_sweep(args, torch, probe, line)
-                roles = split_roles(torch, rank)
                 if line is not None:
                     line["config3_sweep"] = sweep
+            if args.scenario == "auto" and world == 2:
+                roles = split_roles(torch, rank)
+                if line is not None:
                     line["split_roles_device_descriptor"] = roles
             if args.scenario == "auto" and world == 4:
                 sub = run_fanout(args, torch, tokens=65536, steps=min(args.steps, 40), probe=probe)
