@@ -64,7 +64,7 @@ def parse():
     ap.add_argument("--engine", default="tma", choices=["tma", "vec"])
     ap.add_argument("--seed", type=int, default=1)
     ap.add_argument("--pool-blocks", type=int, default=4096, help="slots per pool (the configs use 4,096)")
-    ap.add_argument("--p2p", default="pull", choices=["pull", "pull-gated", "push", "push-tma"],
+    ap.add_argument("--p2p", default="pull-gated", choices=["pull", "pull-gated", "push", "push-tma"],
                     help="N > 1: the decode GPU pulls (TMA loads of peer memory; pull-gated: the READY wait and the "
                          "DONE release inside the copy launch, skv_copy_gated), or the prefill GPU pushes (vector "
                          "engine remote stores, or TMA bulk stores to peer memory)")
