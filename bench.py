@@ -8,9 +8,11 @@ recurrent + conv state (fp32) plus the token ids.  Bytes per sequence B(T) = 24,
 
   N = 1   config 2(a): pool -> pool on one GPU, source and destination block tables independent
           seed-random permutations of two 4,096-block pools.  ONE skv_copy launch per step.
-  N > 1   config 3/5: N/2 prefill -> decode pairs (even rank -> next odd rank), the prefill GPU pushes the
-          sequence straight into the decode GPU's pool through CUDA-IPC peer pointers over NVLink (one
-          skv_copy launch + one completion-flag store), the decode GPU waits on the flag (bounded).
+  N > 1   config 3: N/2 prefill -> decode pairs (even rank -> next odd rank); by default the decode GPU pulls
+          the sequence straight into its own pool over NVLink through CUDA-IPC peer pointers in ONE launch
+          (skv_copy_gated: it waits for the prefill GPU's READY flag and releases DONE on the prefill GPU
+          itself, both bounded); --p2p pull / push / push-tma select the others.  At N = 2 the line adds config
+          3's length sweep and the split-role record, at N = 4 config 4 (fan-out), at N = 8 config 5.
   e2e     park (pool -> pinned host image) + resume (host image -> another pool) through the C ABI, host
           copies inside the timed region: the host-mediated handoff a user of the reference's park path gets.
   --impl reference
