@@ -858,6 +858,7 @@ def host_relay_pairs(args, torch, dist, kg, t: int, seq, role: str, peer: int, a
             step()
     torch.cuda.synchronize()
     dist.barrier()
+    device_align(torch, dist)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     for _ in range(steps):
@@ -978,6 +979,7 @@ def run_pairs(args, torch, tokens: int | None = None, steps: int | None = None, 
         step()
     torch.cuda.synchronize()
     dist.barrier()
+    device_align(torch, dist)
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(n_steps + 1)]
     with Clocks(local) as clk:
         ev[0].record(stream)
@@ -1168,6 +1170,7 @@ def run_fanout(args, torch, tokens: int | None = None, steps: int | None = None,
             step()
         torch.cuda.synchronize()
         dist.barrier()
+        device_align(torch, dist)
         ev = [torch.cuda.Event(enable_timing=True) for _ in range(n_steps + 1)]
         ev[0].record(stream)
         for i in range(n_steps):
@@ -1539,6 +1542,7 @@ def run_mixed(args, torch, probe: dict | None = None) -> dict | None:
     for it in range(warmup + steps):
         dist.barrier()
         torch.cuda.synchronize()
+        device_align(torch, dist)
         h0, h1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in pulls]
@@ -1713,6 +1717,16 @@ def pack_image(torch, ps: skv.PooledSequence):
     return image
 
 
+def device_align(torch, dist) -> None:
+    """Line the GPUs up on the device before a multi-GPU timed region: a one-element all-reduce that the current
+    stream waits for, so each GPU's next operation (the timing event, then the first step) starts when the last rank
+    has reached this point.  Without it the ranks' host skew after the barrier lands in the first timed step (a
+    prefill GPU starts its clock while its decode rank has not launched yet).  Every rank calls it at the same
+    points."""
+    t = torch.ones(1, device="cuda" if torch.cuda.is_available() else "cpu")
+    dist.all_reduce(t)
+
+
 def ranks() -> tuple:
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
     return rank, world, int(os.environ.get("LOCAL_RANK", rank))
@@ -1723,7 +1737,7 @@ def brief(line: dict | None, keys=("value", "ms_per_step", "p50_ms", "p99_ms", "
     if line is None:
         return None
     out = {k: line[k] for k in keys if k in line}
-    for k in ("config", "methods", "roofline", "handoffs", "parks", "port_bound"):
+    for k in ("config", "methods", "roofline", "handoffs", "parks", "port_bound", "phases"):
         if k in line:
             out[k] = line[k]
     return out

@@ -176,6 +176,7 @@ def _rank(rank, world, port, q):
         dist.all_reduce(per, op=dist.ReduceOp.MAX)
         res = bench.summarize_pairs(float(elapsed[0]), per.numpy(), world // 2, 1000, 3)
         # the per-pair verdicts and probe times as the bench gathers them: every rank's value, split by pair
+        bench.device_align(torch, dist)   # every rank takes the same collective before a timed region
         mine_t = torch.tensor([float(rank == 1)])
         every = [torch.zeros_like(mine_t) for _ in range(world)]
         dist.all_gather(every, mine_t)
