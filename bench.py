@@ -77,10 +77,12 @@ def parse():
                          "and config 5 at N = 8 embedded in the same line; sweep = pairs and config 3's sweep only")
     ap.add_argument("--chunk-mb", type=int, default=16,
                     help="fan-out chain: pipeline chunk size (16 / 32 / 64 MB measured 1,936 / 1,910 / 1,869 GB/s)")
-    ap.add_argument("--mixed-order", default="phased", choices=["phased", "phased-unfused", "per-source", "serial"],
+    ap.add_argument("--mixed-order", default="phased",
+                    choices=["phased", "phased-tail", "phased-unfused", "per-source", "serial"],
                     help="config 5: a decode GPU pulls on one stream per source prefill GPU, or one sequence at a "
                          "time, or in port-exclusive phases (phased_schedule; back-to-back runs from one source "
-                         "fused into one launch unless phased-unfused)")
+                         "fused into one launch unless phased-unfused; phased-tail: the last, small phases without "
+                         "hand-over waits, on one stream per source)")
     ap.add_argument("--tuning", default=None,
                     help="copy-engine geometry for this run, STAGES,TILE_BYTES,TMA_CTAS_PER_SM[,VEC_CTAS_PER_SM] "
                          "(skv_set_copy_tuning); default: the library's")
@@ -120,8 +122,9 @@ class Clocks:
     REASONS = {"hw_slowdown": 0x8, "hw_thermal_slowdown": 0x40, "sw_thermal_slowdown": 0x20, "sw_power_cap": 0x4,
                "hw_power_brake_slowdown": 0x80}
 
-    def __init__(self, cuda_index: int):
+    def __init__(self, cuda_index: int, sample: bool = True):
         self.cuda_index = cuda_index
+        self.sample = sample   # False: no polling thread in this process (the other ranks of a multi-GPU run)
         self.samples = []
         self.max_mhz = None
         self._stop = threading.Event()
@@ -137,6 +140,8 @@ class Clocks:
             return nv.nvmlDeviceGetHandleByIndex(self.cuda_index)
 
     def __enter__(self):
+        if not self.sample:
+            return self
         try:
             import pynvml as nv
             nv.nvmlInit()
@@ -248,17 +253,35 @@ def percentiles(ms: list) -> tuple:
     return float(np.percentile(a, 50)), float(np.percentile(a, 99))
 
 
+class quiet_gc:
+    """Python's cyclic garbage collector paused for a timed region (a collection of a large heap can stall the
+    launching thread for milliseconds, and a stalled rank stalls its pair); collected once before and after."""
+
+    def __enter__(self):
+        import gc
+        gc.collect()
+        self.was = gc.isenabled()
+        gc.disable()
+        return self
+
+    def __exit__(self, *a):
+        import gc
+        if self.was:
+            gc.enable()
+
+
 def time_steps(torch, stream, fn, steps: int, warmup: int) -> tuple:
     """W warm-up calls, then K timed calls bracketed by synchronize; per-step CUDA events on `stream`."""
     for _ in range(warmup):
         fn()
     torch.cuda.synchronize()
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(steps + 1)]
-    ev[0].record(stream)
-    for i in range(steps):
-        fn()
-        ev[i + 1].record(stream)
-    torch.cuda.synchronize()
+    with quiet_gc():
+        ev[0].record(stream)
+        for i in range(steps):
+            fn()
+            ev[i + 1].record(stream)
+        torch.cuda.synchronize()
     per = [ev[i].elapsed_time(ev[i + 1]) for i in range(steps)]
     return ev[0].elapsed_time(ev[steps]), per
 
@@ -981,7 +1004,7 @@ def run_pairs(args, torch, tokens: int | None = None, steps: int | None = None, 
     dist.barrier()
     device_align(torch, dist)
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(n_steps + 1)]
-    with Clocks(local) as clk:
+    with Clocks(local, sample=rank == 0) as clk, quiet_gc():
         ev[0].record(stream)
         for i in range(n_steps):
             step()
@@ -1172,11 +1195,12 @@ def run_fanout(args, torch, tokens: int | None = None, steps: int | None = None,
         dist.barrier()
         device_align(torch, dist)
         ev = [torch.cuda.Event(enable_timing=True) for _ in range(n_steps + 1)]
-        ev[0].record(stream)
-        for i in range(n_steps):
-            step()
-            ev[i + 1].record(stream)
-        torch.cuda.synchronize()
+        with quiet_gc():
+            ev[0].record(stream)
+            for i in range(n_steps):
+                step()
+                ev[i + 1].record(stream)
+            torch.cuda.synchronize()
         dist.barrier()
         per = torch.tensor([ev[i].elapsed_time(ev[i + 1]) for i in range(n_steps)], device="cuda")
         tot = torch.tensor([ev[0].elapsed_time(ev[n_steps])], device="cuda")
@@ -1383,6 +1407,25 @@ def phased_schedule(plan: dict, sizes: list, world: int) -> dict:
                                      [r for r in range(world) if r % 2 == 1])
 
 
+TAIL_FRAC = 0.05   # phased-tail: a phase whose largest run moves less than this share of the busiest port's bytes
+
+
+def tail_start(sched: dict, frac: float = TAIL_FRAC) -> int | None:
+    """The first phase of the schedule's tail: the longest run of LAST phases whose largest run (over every
+    destination) moves less than `frac` of the busiest port's bytes; None when the last phase is not that small.
+    Waits point only at earlier phases, so no run before the tail waits for a run inside it."""
+    weight = {}
+    for runs in sched["runs"].values():
+        for r in runs:
+            weight[r["phase"]] = max(weight.get(r["phase"], 0), r["hi"] - r["lo"])
+    start = None
+    for k in sorted(weight, reverse=True):
+        if weight[k] >= frac * sched["bound_bytes"]:
+            break
+        start = k
+    return start
+
+
 def phase_runs(rank: int, plan: dict, sizes: list, segs_of: dict, world: int) -> list:
     """Decode GPU `rank`'s runs under phased_schedule, ready to launch (handoff_schedule.launch_list).  `sizes[i]`
     = sequence i's bytes (all 64, for the global schedule); `segs_of[i]` = the segments moving sequence i into this
@@ -1476,7 +1519,7 @@ def run_mixed(args, torch, probe: dict | None = None) -> dict | None:
     held = SeqSet(torch, kg, [lengths[i] for i in (mine_in if decode else mine_out)], args.seed + 7 * rank,
                   fill=not decode)
     slots = SeqSet(torch, kg, [SLOT_TOKENS] * (2 * SERVE_SLOTS), args.seed + 7 * rank + 3, fill=True) if decode else None
-    phased = args.mixed_order in ("phased", "phased-unfused")
+    phased = args.mixed_order in ("phased", "phased-tail", "phased-unfused")
     flags = None
     if decode and phased:            # one 8-byte word per run of this GPU's phased order (phased_schedule)
         flags = skv.Pool(local, 1, 4096)
@@ -1508,12 +1551,15 @@ def run_mixed(args, torch, probe: dict | None = None) -> dict | None:
         pulls.append((i, (skv.Segment * len(segs))(*segs), len(segs)))
         segs_of[i] = segs
     runs, peer_flags = [], {}
+    tail_from = None   # phased-tail: the first phase run without hand-overs, on per-source streams
     if decode and phased:
         stream_bytes = lambda t: (2 * kg.n_qsa * kg.pages(t) * kg.page_bytes + kg.gdn_bytes  # noqa: E731
                                   + 16 * ((4 * t + 15) // 16))
         order = phase_runs(rank, plan, [stream_bytes(t) for t in lengths], segs_of, world)
-        if args.mixed_order == "phased":
+        if args.mixed_order in ("phased", "phased-tail"):
             order = handoff_schedule.fuse_runs(order)
+        if args.mixed_order == "phased-tail":
+            tail_from = tail_start(phased_schedule(plan, [stream_bytes(t) for t in lengths], world))
         for run in order:
             pieces = run["pieces"]
             arrays = [((skv.Segment * len(pieces[a:a + skv.MAX_SEGMENTS]))(*pieces[a:a + skv.MAX_SEGMENTS]),
@@ -1539,6 +1585,7 @@ def run_mixed(args, torch, probe: dict | None = None) -> dict | None:
     windows = []   # (handoff window, park window) per timed step, this rank
     idle = []      # phased: per timed step, the window minus this GPU's copy time
     timeline = []  # phased, --timeline: the last timed step's runs on this GPU
+    gc_pause = quiet_gc().__enter__()   # paused for the whole step loop (resumed after it)
     for it in range(warmup + steps):
         dist.barrier()
         torch.cuda.synchronize()
@@ -1553,7 +1600,19 @@ def run_mixed(args, torch, probe: dict | None = None) -> dict | None:
             # this GPU's runs in phase order on one stream; a run from a prefill GPU another decode GPU read
             # before waits for that GPU's signal, and each run signals the next reader of its source
             rev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in runs]
+            tail_streams = set()
             for j, (run, (a, b)) in enumerate(zip(runs, rev)):
+                if tail_from is not None and run["phase"] >= tail_from:
+                    # the tail: no hand-over; each run on its source's stream, after this GPU's exclusive runs
+                    st = source_stream[run["src"]]
+                    if st not in tail_streams:
+                        st.wait_stream(stream)
+                        tail_streams.add(st)
+                    a.record(st)
+                    for arr, n in run["arrays"]:
+                        skv.check(L.skv_copy(arr, n, skv.COPY_TMA, st.cuda_stream))
+                    b.record(st)
+                    continue
                 if run["wait"] is not None:
                     skv.check(L.skv_wait_flag(flags.base + 8 * run["wait"], it + 1, 5_000_000_000, sp))
                 a.record(stream)
@@ -1563,6 +1622,8 @@ def run_mixed(args, torch, probe: dict | None = None) -> dict | None:
                 if run["signal"] is not None:
                     r, idx = run["signal"]
                     skv.check(L.skv_signal(peer_flags[r] + 8 * idx, it + 1, sp))
+            for st in tail_streams:
+                stream.wait_stream(st)
             first = {i: rev[j][0] for j in reversed(range(len(runs))) for i in runs[j]["starts"]}
             last = {i: rev[j][1] for j in range(len(runs)) for i in runs[j]["ends"]}
             ev = [(first[i], last[i]) for i, _, _ in pulls]
@@ -1594,6 +1655,7 @@ def run_mixed(args, torch, probe: dict | None = None) -> dict | None:
                 idle.append(h0.elapsed_time(h1) - sum(a.elapsed_time(b) for a, b in rev))
                 timeline = [[round(h0.elapsed_time(a), 3), round(h0.elapsed_time(b), 3), r["hi"] - r["lo"],
                              r["src"], r["phase"], r["wait"] is not None] for r, (a, b) in zip(runs, rev)]
+    gc_pause.__exit__()
     skv.set_copy_tuning(*tuning)
     status = torch.tensor([float(skv.query_status(local) != 0)], device="cuda")
     dist.all_reduce(status, op=dist.ReduceOp.MAX)

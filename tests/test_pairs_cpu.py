@@ -321,3 +321,32 @@ def test_fused_runs_move_the_same_bytes_with_the_same_hand_overs(world, seed):
         for a, b in zip(fused, fused[1:]):
             assert not (a["src"] == b["src"] and a["signal"] is None and b["wait"] is None)
     assert fused_any or world == 4
+
+
+@pytest.mark.parametrize("world,seed", [(8, 1), (8, 5), (8, 9), (4, 2)])
+def test_tail_phases_are_a_suffix_no_exclusive_run_waits_on(world, seed):
+    """phased-tail drops the hand-overs of the last, small phases.  That is safe only if no run before the tail
+    waits for a signal that a tail run sends: every run's wait is released by a run of an earlier phase."""
+    kg = skv.KvGeometry()
+    plan = bench.mixed_plan(world, seed)
+    sizes = [2 * kg.n_qsa * kg.pages(t) * kg.page_bytes + kg.gdn_bytes + 16 * ((4 * t + 15) // 16)
+             for t in plan["lengths"]]
+    sched = bench.phased_schedule(plan, sizes, world)
+    start = bench.tail_start(sched)
+    phases = sorted({r["phase"] for runs in sched["runs"].values() for r in runs})
+    if start is None:
+        return
+    assert start in phases and all(p >= start for p in phases[phases.index(start):])
+    big = max(r["hi"] - r["lo"] for runs in sched["runs"].values() for r in runs if r["phase"] >= start)
+    assert big < bench.TAIL_FRAC * sched["bound_bytes"]
+    releaser = {}
+    for d, runs in sched["runs"].items():
+        for r in runs:
+            if r["signal"] is not None:
+                releaser[r["signal"]] = r["phase"]
+    for d, runs in sched["runs"].items():
+        for r in runs:
+            if r["wait"] is not None:
+                assert releaser[(d, r["wait"])] < r["phase"]
+                if r["phase"] < start:
+                    assert releaser[(d, r["wait"])] < start
