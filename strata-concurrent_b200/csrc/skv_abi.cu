@@ -363,11 +363,11 @@ int skv_copy(const skv_segment* segs, int n_segs, int engine, void* stream) {
 
 int skv_copy_gated(const skv_segment* segs, int n_segs, const uint64_t* wait_flag, uint64_t wait_value,
                    uint64_t timeout_ns, uint64_t* done_flag, uint64_t done_value, void* stream) {
-    DeviceCtx* ctx = current_ctx();
-    if (!ctx) return SKV_ECUDA;
     if ((reinterpret_cast<uintptr_t>(wait_flag) | reinterpret_cast<uintptr_t>(done_flag)) & 7u)
         return fail(SKV_EINVAL, "skv_copy_gated: flags must be 8-byte aligned");
     if (timeout_ns > 60ull * 1000000000ull) return fail(SKV_EINVAL, "skv_copy_gated: timeout must be at most 60 s");
+    DeviceCtx* ctx = current_ctx();
+    if (!ctx) return SKV_ECUDA;
     CopyPlan plan;
     uint64_t tiles = 0;
     if (const int rc = build_plan(segs, n_segs, SKV_COPY_TMA, plan, tiles)) return rc;

@@ -140,3 +140,14 @@ def test_allocator_under_threads_never_hands_out_a_held_block():
     assert not errors, errors[0]
     assert p.free_count() == 256 and not held
     p.close()
+
+
+def test_gated_copy_refuses_bad_flags_before_touching_a_device():
+    """skv_copy_gated checks its flags and its timeout before anything reaches a device."""
+    seg = (skv.Segment * 1)(skv.segment(0x1000, 0x2000, 4096))
+    L = skv.lib()
+    assert L.skv_copy_gated(seg, 1, 0x1004, 1, 0, None, 0, None) == skv.EINVAL          # misaligned wait flag
+    assert "8-byte aligned" in L.skv_last_error().decode()
+    assert L.skv_copy_gated(seg, 1, None, 0, 0, 0x2002, 1, None) == skv.EINVAL          # misaligned done flag
+    assert L.skv_copy_gated(seg, 1, 0x1000, 1, 61 * 10 ** 9, None, 0, None) == skv.EINVAL   # timeout past 60 s
+    assert "60 s" in L.skv_last_error().decode()
