@@ -1002,9 +1002,11 @@ def run_pairs(args, torch, tokens: int | None = None, steps: int | None = None, 
         step()
     torch.cuda.synchronize()
     dist.barrier()
-    device_align(torch, dist)
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(n_steps + 1)]
+    # host-side preparation (the collection, the clock sampler's start) first, then the device-side alignment, then
+    # at once the start event and the steps: anything a host does after the alignment is skew in the first step
     with Clocks(local, sample=rank == 0) as clk, quiet_gc():
+        device_align(torch, dist)
         ev[0].record(stream)
         for i in range(n_steps):
             step()
@@ -1193,9 +1195,9 @@ def run_fanout(args, torch, tokens: int | None = None, steps: int | None = None,
             step()
         torch.cuda.synchronize()
         dist.barrier()
-        device_align(torch, dist)
         ev = [torch.cuda.Event(enable_timing=True) for _ in range(n_steps + 1)]
         with quiet_gc():
+            device_align(torch, dist)   # after the collection: nothing of the host's lands in the first step
             ev[0].record(stream)
             for i in range(n_steps):
                 step()
