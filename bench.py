@@ -86,6 +86,9 @@ def parse():
     ap.add_argument("--tuning", default=None,
                     help="copy-engine geometry for this run, STAGES,TILE_BYTES,TMA_CTAS_PER_SM[,VEC_CTAS_PER_SM] "
                          "(skv_set_copy_tuning); default: the library's")
+    ap.add_argument("--relay-mb", type=int, default=RELAY_CHUNK_BYTES >> 20, help="N = 1 e2e relay: piece size")
+    ap.add_argument("--relay-lanes", type=int, default=1, choices=[1, 2],
+                    help="N = 1 e2e relay: streams per direction the pieces alternate over")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-length-sweep", action="store_true",
                     help="N = 1: leave out the 1K / 4K / 128K pool->pool lines the headline line carries")
@@ -335,21 +338,24 @@ def pcie_probe(torch, nbytes: int = 1 << 30, reps: int = 5) -> dict:
 RELAY_CHUNK_BYTES = 32 << 20
 
 
-def relay_pieces(park_segs: list, resume_segs: list) -> list:
+def relay_pieces(park_segs: list, resume_segs: list, piece_bytes: int = RELAY_CHUNK_BYTES) -> list:
     """A pipelined host relay's chunks: every park segment and its resume twin cut into the same pieces of at most
-    RELAY_CHUNK_BYTES, as (park piece, resume piece) pairs in order."""
+    `piece_bytes`, as (park piece, resume piece) pairs in order."""
     out = []
     for p, r in zip(park_segs, resume_segs):
-        out += list(zip(skv.split_segment(p, RELAY_CHUNK_BYTES), skv.split_segment(r, RELAY_CHUNK_BYTES)))
+        out += list(zip(skv.split_segment(p, piece_bytes), skv.split_segment(r, piece_bytes)))
     return out
 
 
-def e2e_park_resume(torch, kg, src: SeqOnGpu, dst: SeqOnGpu, steps: int, warmup: int, side_steps: int) -> dict:
+def e2e_park_resume(torch, kg, src: SeqOnGpu, dst: SeqOnGpu, steps: int, warmup: int, side_steps: int,
+                    piece_bytes: int = RELAY_CHUNK_BYTES, lanes: int = 1) -> dict:
     """Host-mediated handoff through the C ABI: park to pinned host, resume into another table.
 
     relay (the reported e2e, fixed in advance): skv_park and skv_resume chunk by chunk on two streams - the park
            of chunk c+1 (device -> host) runs while the resume of chunk c (host -> device) runs, so both PCIe
-           directions are busy at once.  Timed over `steps` steps.
+           directions are busy at once.  Timed over `steps` steps.  lanes = 2 alternates the pieces over two
+           streams per direction, so piece c+1's gather kernel runs beside piece c's device-to-host copy (and piece
+           c's scatter beside piece c+1's host-to-device copy) instead of holding the copy engine idle.
     staged / direct (extra keys): one skv_park then one skv_resume of the whole sequence, staged through device
            memory or with the kernel reading and writing mapped host memory.  Timed over `side_steps` steps."""
     off = skv.image_offsets(kg, src.tokens, kg.n_qsa)
@@ -358,31 +364,37 @@ def e2e_park_resume(torch, kg, src: SeqOnGpu, dst: SeqOnGpu, steps: int, warmup:
     staging_b = torch.empty(off["total"] + 256 * 64, dtype=torch.uint8, device="cuda")
     stream = torch.cuda.current_stream()
     side = torch.cuda.Stream()
+    park_streams = [stream] + [torch.cuda.Stream() for _ in range(lanes - 1)]
+    resume_streams = [side] + [torch.cuda.Stream() for _ in range(lanes - 1)]
     park_segs = skv.pack_segments(src.ps, host.ptr)
     resume_segs = skv.unpack_segments(host.ptr, dst.ps)
-    chunks = relay_pieces(park_segs, resume_segs)
+    chunks = relay_pieces(park_segs, resume_segs, piece_bytes)
     chunk_off = []
     at = 0
     for pp, _ in chunks:
         chunk_off.append(at)
         at += (pp.bytes + 255) & ~255
     parked = [torch.cuda.Event() for _ in chunks]
-    resumed = torch.cuda.Event()
+    resumed = [torch.cuda.Event() for _ in resume_streams]
     parity, modes, results = {}, {}, {}
     b = kg.metric_bytes(src.tokens)
     for mode, name, n_steps in ((skv.PARK_STAGED, "relay", steps), (skv.PARK_STAGED, "staged", side_steps),
                                 (skv.PARK_DIRECT, "direct", side_steps)):
         if name == "relay":
             def step():
+                for ps in park_streams[1:]:
+                    ps.wait_stream(stream)   # the previous step (and its resumes) finished before any park
                 for k, (pp, rp) in enumerate(chunks):
+                    ps, rs = park_streams[k % lanes], resume_streams[k % lanes]
                     a = staging.data_ptr() + chunk_off[k]
-                    skv.park([pp], mode, a, staging.numel() - chunk_off[k], stream)
-                    parked[k].record(stream)
-                    side.wait_event(parked[k])
+                    skv.park([pp], mode, a, staging.numel() - chunk_off[k], ps)
+                    parked[k].record(ps)
+                    rs.wait_event(parked[k])
                     b2 = staging_b.data_ptr() + chunk_off[k]
-                    skv.resume([rp], mode, b2, staging_b.numel() - chunk_off[k], side)
-                resumed.record(side)
-                stream.wait_event(resumed)
+                    skv.resume([rp], mode, b2, staging_b.numel() - chunk_off[k], rs)
+                for ev_r, rs in zip(resumed, resume_streams):
+                    ev_r.record(rs)
+                    stream.wait_event(ev_r)
         else:
             def step():
                 skv.park(park_segs, mode, staging, staging.numel(), stream)
@@ -401,7 +413,7 @@ def e2e_park_resume(torch, kg, src: SeqOnGpu, dst: SeqOnGpu, steps: int, warmup:
     host.close()
     r = results["relay"]
     return {"value": round(r["value"], 3), "unit": UNIT, "h2d_bytes_per_step": b, "d2h_bytes_per_step": b,
-            "mode": "relay", "steps": r["steps"], "p50_ms": round(r["p50_ms"], 3), "p99_ms": round(r["p99_ms"], 3),
+            "mode": "relay", "piece_mb": piece_bytes >> 20, "lanes": lanes, "steps": r["steps"], "p50_ms": round(r["p50_ms"], 3), "p99_ms": round(r["p99_ms"], 3),
             "pcie_gbs_both_directions": round(r["pcie_gbs_both_directions"], 3),
             "other_modes_gbs": {k: v for k, v in modes.items() if k != "relay"}, "other_modes_steps": side_steps,
             "api": "skv_park + skv_resume (C ABI), pinned host image, 32 MB pieces on two streams",
@@ -636,7 +648,8 @@ def run_single(args, torch) -> None:
         line["length_sweep"] = [pool_to_pool_length(args, torch, kg, n, engine, hbm)
                                 for n in SWEEP_TOKENS if n != t]
     if not args.no_e2e:
-        e2e = e2e_park_resume(torch, kg, src, dst, args.steps, max(3, args.warmup), max(3, args.steps // 4))
+        e2e = e2e_park_resume(torch, kg, src, dst, args.steps, max(3, args.warmup), max(3, args.steps // 4),
+                              args.relay_mb << 20, args.relay_lanes)
         pcie = pcie_probe(torch)
         e2e["pcie_peak"] = pcie
         # the relay keeps both directions busy, so its bound is the two-direction probe
