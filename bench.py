@@ -87,7 +87,7 @@ def parse():
                     help="copy-engine geometry for this run, STAGES,TILE_BYTES,TMA_CTAS_PER_SM[,VEC_CTAS_PER_SM] "
                          "(skv_set_copy_tuning); default: the library's")
     ap.add_argument("--relay-mb", type=int, default=RELAY_CHUNK_BYTES >> 20, help="N = 1 e2e relay: piece size")
-    ap.add_argument("--relay-lanes", type=int, default=1, choices=[1, 2],
+    ap.add_argument("--relay-lanes", type=int, default=2, choices=[1, 2],
                     help="N = 1 e2e relay: streams per direction the pieces alternate over")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-length-sweep", action="store_true",
