@@ -83,6 +83,10 @@ def parse():
                          "time, or in port-exclusive phases (phased_schedule; back-to-back runs from one source "
                          "fused into one launch unless phased-unfused; phased-tail: the last, small phases without "
                          "hand-over waits, on one stream per source)")
+    ap.add_argument("--handover", default="launch", choices=["launch", "gated"],
+                    help="config 5, phased orders: a run waits for its source's hand-over and signals the next "
+                         "reader with launches of their own around its copy (launch), or inside the copy launch "
+                         "itself (gated: skv_copy_gated; a run's time then includes its wait)")
     ap.add_argument("--tuning", default=None,
                     help="copy-engine geometry for this run, STAGES,TILE_BYTES,TMA_CTAS_PER_SM[,VEC_CTAS_PER_SM] "
                          "(skv_set_copy_tuning); default: the library's")
@@ -1511,7 +1515,8 @@ def run_mixed(args, torch, probe: dict | None = None) -> dict | None:
       phased      (default) port-exclusive phases from phased_schedule: one stream, each prefill GPU read by one
                   decode GPU at a time, hand-overs by device flags (skv_signal / skv_wait_flag); back-to-back runs
                   from one source with no hand-over between them are one launch (handoff_schedule.fuse_runs;
-                  phased-unfused keeps every run a launch of its own);
+                  phased-unfused keeps every run a launch of its own; --handover gated moves each run's wait
+                  and signal inside its copy launch, skv_copy_gated);
       per-source  one stream per source prefill GPU, one skv_copy per sequence, all sources at once;
       serial      one skv_copy per sequence, back to back.
 
@@ -1535,6 +1540,7 @@ def run_mixed(args, torch, probe: dict | None = None) -> dict | None:
                   fill=not decode)
     slots = SeqSet(torch, kg, [SLOT_TOKENS] * (2 * SERVE_SLOTS), args.seed + 7 * rank + 3, fill=True) if decode else None
     phased = args.mixed_order in ("phased", "phased-tail", "phased-unfused")
+    gated = phased and args.handover == "gated"
     flags = None
     if decode and phased:            # one 8-byte word per run of this GPU's phased order (phased_schedule)
         flags = skv.Pool(local, 1, 4096)
@@ -1628,15 +1634,28 @@ def run_mixed(args, torch, probe: dict | None = None) -> dict | None:
                         skv.check(L.skv_copy(arr, n, skv.COPY_TMA, st.cuda_stream))
                     b.record(st)
                     continue
-                if run["wait"] is not None:
-                    skv.check(L.skv_wait_flag(flags.base + 8 * run["wait"], it + 1, 5_000_000_000, sp))
+                wait = flags.base + 8 * run["wait"] if run["wait"] is not None else None
+                done = peer_flags[run["signal"][0]] + 8 * run["signal"][1] if run["signal"] is not None else None
+                if gated:
+                    # the wait inside the run's first launch, the release inside its last (skv_copy_gated)
+                    a.record(stream)
+                    last = len(run["arrays"]) - 1
+                    for q, (arr, n) in enumerate(run["arrays"]):
+                        w, d = (wait if q == 0 else None), (done if q == last else None)
+                        if w is None and d is None:
+                            skv.check(L.skv_copy(arr, n, skv.COPY_TMA, sp))
+                        else:
+                            skv.check(L.skv_copy_gated(arr, n, w, it + 1, 5_000_000_000, d, it + 1, sp))
+                    b.record(stream)
+                    continue
+                if wait is not None:
+                    skv.check(L.skv_wait_flag(wait, it + 1, 5_000_000_000, sp))
                 a.record(stream)
                 for arr, n in run["arrays"]:
                     skv.check(L.skv_copy(arr, n, skv.COPY_TMA, sp))
                 b.record(stream)
-                if run["signal"] is not None:
-                    r, idx = run["signal"]
-                    skv.check(L.skv_signal(peer_flags[r] + 8 * idx, it + 1, sp))
+                if done is not None:
+                    skv.check(L.skv_signal(done, it + 1, sp))
             for st in tail_streams:
                 stream.wait_stream(st)
             first = {i: rev[j][0] for j in reversed(range(len(runs))) for i in runs[j]["starts"]}
@@ -1700,8 +1719,8 @@ def run_mixed(args, torch, probe: dict | None = None) -> dict | None:
     facts = {"lat": lat, "landed": landed, "park_ms": [w[1] for w in windows], "hand_ms": [w[0] for w in windows],
              "bytes_in": sum(kg.metric_bytes(lengths[i]) for i in mine_in), "decode": decode,
              "idle_ms": round(float(np.mean(idle)), 3) if idle else None, "timeline": timeline, "rank": rank,
-             "launches": (sum(len(r["arrays"]) + (r["wait"] is not None) + (r["signal"] is not None) for r in runs)
-                          if phased else len(pulls))}
+             "launches": (sum(len(r["arrays"]) + (not gated) * ((r["wait"] is not None) + (r["signal"] is not None))
+                              for r in runs) if phased else len(pulls))}
     allf = [None] * world
     dist.all_gather_object(allf, facts)
     torch.cuda.synchronize()
@@ -1738,7 +1757,7 @@ def run_mixed(args, torch, probe: dict | None = None) -> dict | None:
                                    f"resume from pinned host memory",
                        "sequences": MIXED_SEQUENCES, "mean_tokens": round(float(np.mean(lengths)), 1),
                        "bytes_per_step": total, "serve_slots": SERVE_SLOTS, "slot_tokens": SLOT_TOKENS,
-                       "order": args.mixed_order,
+                       "order": args.mixed_order, **({"handover": args.handover} if phased else {}),
                        "parallelism": f"{world // 2} prefill + {world // 2} decode"},
             **({"timeline": {f["rank"]: f["timeline"] for f in dec}} if args.timeline else {}),
             **({"phases": phase_summary([f["timeline"] for f in dec])} if phased else {}),
