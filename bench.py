@@ -1130,6 +1130,12 @@ def split_roles(torch, rank: int) -> list | None:
                 pub = re.search(r"publish \(pack into HBM \+ descriptor\) ([0-9.]+) ms; fastest claim-to-release "
                                 r"\(publish, DONE, decode mount, ACK, release\) ([0-9.]+) ms for ([0-9]+) payload bytes", out)
                 mnt = re.search(r"read the slot \+ mount from the peer's HBM ([0-9.]+) ms", out)
+                phases = {side: dict(zip(("prepare_ms", "issue_ms", "complete_ms", "total_ms"),
+                                         (float(x) for x in m.groups())))
+                          for side, m in (("pack", re.search(r"pack phases prepare ([0-9.]+) issue ([0-9.]+) complete "
+                                                             r"([0-9.]+) total ([0-9.]+) ms", out)),
+                                          ("mount", re.search(r"mount phases prepare ([0-9.]+) issue ([0-9.]+) complete "
+                                                              r"([0-9.]+) total ([0-9.]+) ms", out))) if m}
                 checks = [int(c) for c in re.findall(r"([0-9]+) checks passed", out)]
                 row = {"tokens": t, "rc": r.returncode, "parity": r.returncode == 0 and "both instances passed" in out,
                        "checks": sum(checks)}
@@ -1138,6 +1144,8 @@ def split_roles(torch, rank: int) -> list | None:
                     row.update({"payload_bytes": nbytes, "publish_ms": float(pub.group(1)),
                                 "mount_ms": float(mnt.group(1)), "claim_to_release_ms": float(pub.group(2)),
                                 "mount_gbs_over_nvlink": round(nbytes / (float(mnt.group(1)) / 1e3) / 1e9, 1)})
+                if phases:
+                    row["phases"] = phases
                 if r.returncode:
                     row["tail"] = (out + r.stderr)[-400:]
                 rows.append(row)

@@ -69,4 +69,14 @@ ConversationRestore conversation_wire_mount_device(const uint8_t* payload, uint6
                                                    const WireExpect& expect, SavedConversation& meta,
                                                    WireDecoded& info, std::string& error);
 
+/// Host-clock phases of this thread's last successful conversation_wire_pack_device or
+/// conversation_wire_mount_device, in milliseconds.  prepare: validation, planning, the header and record stream
+/// (written, or read from the payload and decoded), and the wait for work already queued on the session's devices;
+/// issue: enqueueing every copy (for a host destination the per-device copies are waited for here too); complete:
+/// waiting for the device copies to land and reading the status word (for a host destination: the payload hash).
+struct WireDevicePhases {
+    double prepare_ms = 0, issue_ms = 0, complete_ms = 0, total_ms = 0;
+};
+WireDevicePhases conversation_wire_device_last_phases();
+
 }  // namespace strata::core

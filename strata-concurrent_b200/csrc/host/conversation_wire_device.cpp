@@ -22,6 +22,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <chrono>
 #include <cstring>
 #include <functional>
 #include <map>
@@ -227,6 +228,25 @@ bool launch_all(const std::vector<skv_segment>& segs, std::string& error) {
     return true;
 }
 
+thread_local WireDevicePhases t_last_phases;
+
+/// Host-clock marks of one pack or mount; finish() publishes them as this thread's last phases.  A call that fails
+/// publishes nothing (the previous record stays).
+class PhaseClock {
+public:
+    PhaseClock() : t0_(std::chrono::steady_clock::now()), prepared_(t0_), enqueued_(t0_) {}
+    void mark_prepared() { prepared_ = enqueued_ = std::chrono::steady_clock::now(); }
+    void mark_enqueued() { enqueued_ = std::chrono::steady_clock::now(); }
+    void finish() {
+        const auto end = std::chrono::steady_clock::now();
+        auto ms = [](auto a, auto b) { return std::chrono::duration<double, std::milli>(b - a).count(); };
+        t_last_phases = WireDevicePhases{ms(t0_, prepared_), ms(prepared_, enqueued_), ms(enqueued_, end), ms(t0_, end)};
+    }
+
+private:
+    std::chrono::steady_clock::time_point t0_, prepared_, enqueued_;
+};
+
 bool status_clean(int device, std::string& error) {
     uint32_t status = 0;
     if (skv_query_status(device, nullptr, &status) != SKV_OK) return pfail(error, skv_last_error());
@@ -258,6 +278,7 @@ bool conversation_wire_pack_device(const ConversationView& view, const SessionSt
                                    const ConversationStageSet& stages, const ModelGeometry& g, const QsaState& draft,
                                    const WireIdentity& identity, uint8_t* dst, uint64_t capacity, WirePlan& plan,
                                    WireEncoded& out, std::string& error, const WireDeviceOptions& opt) {
+    PhaseClock phases;
     SavedConversation shape;
     Side side;
     std::vector<wire_detail::PlannedBlob> blobs;
@@ -305,15 +326,25 @@ bool conversation_wire_pack_device(const ConversationView& view, const SessionSt
     if (on_device) {
         const DeviceScope on(dst_device);
         if (!device_sync(error)) return false;   // the session's producers are done before the reads
-        // only the pads between blobs (and after the last) need zeros: every other pool byte is gathered
-        std::vector<std::pair<uint64_t, uint64_t>> pads;
+        phases.mark_prepared();
+        // one byte-range launch: the pads between blobs (and after the last; every other pool byte is gathered)
+        // and the pieces too short or unaligned for the bulk engines
+        std::vector<skv::ByteRange> small;
         uint64_t cursor = p.blob_pool_off;
         for (const Placed& pl : placed) {
-            if (pl.at > cursor) pads.emplace_back(cursor, pl.at - cursor);
+            if (pl.at > cursor) small.push_back({dst + cursor, nullptr, pl.at - cursor});
             cursor = std::max(cursor, pl.at + pl.piece->bytes);
         }
-        if (p.total_bytes > cursor) pads.emplace_back(cursor, p.total_bytes - cursor);
-        if (skv::zero_ranges(dst, pads, nullptr) != SKV_OK) return pfail(error, skv_last_error());
+        if (p.total_bytes > cursor) small.push_back({dst + cursor, nullptr, p.total_bytes - cursor});
+        std::vector<size_t> large;
+        for (size_t i : direct) {
+            const Piece& pc = *placed[i].piece;
+            if (pc.bytes <= skv::kByteRangeMaxBytes)
+                small.push_back({dst + placed[i].at, static_cast<const uint8_t*>(pc.dev.base) + pc.from, pc.bytes});
+            else
+                large.push_back(i);
+        }
+        if (skv::byte_ranges(small, nullptr) != SKV_OK) return pfail(error, skv_last_error());
         if (!cuda_ok(cudaMemcpyAsync(dst, records.data(), records.size(), cudaMemcpyHostToDevice, nullptr), error,
                      "records"))
             return false;
@@ -321,7 +352,7 @@ bool conversation_wire_pack_device(const ConversationView& view, const SessionSt
         std::vector<skv_segment> segs;
         for (size_t i : by_device[dst_device]) segs.push_back(segment_of(*placed[i].piece, dst + placed[i].at));
         if (!launch_all(segs, error)) return false;
-        for (size_t i : direct) {
+        for (size_t i : large) {
             const Piece& pc = *placed[i].piece;
             if (!cuda_ok(cudaMemcpyAsync(dst + placed[i].at, static_cast<const uint8_t*>(pc.dev.base) + pc.from,
                                          pc.bytes, cudaMemcpyDeviceToDevice, nullptr),
@@ -334,9 +365,11 @@ bool conversation_wire_pack_device(const ConversationView& view, const SessionSt
                          error, "host blob copy"))
                 return false;
         }
+        phases.mark_enqueued();
         if (!cuda_ok(cudaStreamSynchronize(nullptr), error, "synchronize") ||
             (!segs.empty() && !status_clean(dst_device, error)))
             return false;
+        phases.finish();
         plan = p;
         out.bytes = p.total_bytes;
         out.payload_hash = 0;
@@ -346,6 +379,7 @@ bool conversation_wire_pack_device(const ConversationView& view, const SessionSt
     }
 
     // host destination: mark what each step writes, so every other pool byte is zeroed exactly once
+    phases.mark_prepared();
     std::vector<std::pair<uint64_t, uint64_t>> written;   // [begin, end) absolute
     for (auto& [device, idx] : by_device) {
         const DeviceScope on(device);
@@ -404,12 +438,14 @@ bool conversation_wire_pack_device(const ConversationView& view, const SessionSt
         cursor = std::max(cursor, b);
     }
     if (p.total_bytes > cursor) std::memset(dst + cursor, 0, p.total_bytes - cursor);
+    phases.mark_enqueued();   // the host target's copies wait per device above: they count as enqueue time
 
     plan = p;
     out.bytes = p.total_bytes;
     out.payload_hash = opt.hash ? fnv1a64(dst, p.total_bytes) : 0;
     out.blob_pool_bytes = p.blob_pool_bytes;
     out.blobs = blobs.size();
+    phases.finish();
     return true;
 }
 
@@ -453,7 +489,8 @@ struct MountBatch {
         const void* src;
         uint64_t bytes;
     };
-    std::vector<Plain> plain;
+    std::vector<Plain> plain;                  // copy-engine copies (the host-authoritative K/V of streamed layers)
+    std::vector<skv::ByteRange> small;         // device-to-device pieces too short or unaligned for the engines
     std::vector<std::function<bool(std::string&)>> after;
 
     /// src (device payload) -> dst through `d` (paged or contiguous).
@@ -475,18 +512,25 @@ struct MountBatch {
             sg.dst = dst;
             tma.push_back(sg);
         } else {
-            plain.push_back(Plain{dst, src, bytes});
+            add_device(dst, src, bytes);
         }
+    }
+    /// A device-to-device piece outside the engines' alignment: a byte-range write, or a copy when it is large.
+    void add_device(void* dst, const void* src, uint64_t bytes) {
+        if (!bytes) return;
+        if (bytes <= skv::kByteRangeMaxBytes)
+            small.push_back({static_cast<uint8_t*>(dst), static_cast<const uint8_t*>(src), bytes});
+        else
+            plain.push_back(Plain{dst, src, bytes});
     }
     void add_plain(void* dst, const void* src, uint64_t bytes) {
         if (bytes) plain.push_back(Plain{dst, src, bytes});
     }
 
-    bool run(int device, std::string& error) {
+    /// Enqueue everything on `device`'s legacy stream (phases: issue marked after the last enqueue).
+    bool issue(int device, std::string& error) {
         const DeviceScope on(device);
-        int dev = 0;
-        if (!cuda_ok(cudaGetDevice(&dev), error, "cudaGetDevice")) return false;
-        if (skv_clear_status(dev, nullptr) != SKV_OK) return pfail(error, skv_last_error());
+        if (skv_clear_status(device, nullptr) != SKV_OK) return pfail(error, skv_last_error());
         for (auto* list : {&tma, &vec}) {
             const int engine = list == &tma ? SKV_COPY_TMA : SKV_COPY_VEC;
             for (size_t i = 0; i < list->size(); i += SKV_COPY_MAX_SEGMENTS) {
@@ -495,14 +539,21 @@ struct MountBatch {
                     return pfail(error, std::string("mount copy: ") + skv_last_error());
             }
         }
+        if (skv::byte_ranges(small, nullptr) != SKV_OK) return pfail(error, std::string("mount copy: ") + skv_last_error());
         for (const Plain& p : plain)
             if (!cuda_ok(cudaMemcpyAsync(p.dst, p.src, p.bytes, cudaMemcpyDefault, nullptr), error, "mount copy"))
                 return false;
         for (auto& fn : after)
             if (!fn(error)) return false;
-        if (!cuda_ok(cudaStreamSynchronize(nullptr), error, "synchronize")) return false;
-        return status_clean(dev, error);
+        return true;
     }
+    /// Wait for what issue() enqueued and read the device status.
+    static bool complete(int device, std::string& error) {
+        const DeviceScope on(device);
+        if (!cuda_ok(cudaStreamSynchronize(nullptr), error, "synchronize")) return false;
+        return status_clean(device, error);
+    }
+    bool run(int device, std::string& error) { return issue(device, error) && complete(device, error); }
 };
 
 /// One layer's K/V from the payload into `st` (validated already): the mount twin of enqueue_kv_restore.
@@ -572,7 +623,7 @@ void mount_running(const ConversationCheckpoint& c, const uint8_t* payload, cons
         const QsaState& st = owned_layer(ss, j);
         if (tails) b.add(tails + j * z.tail, flat(st.idx_tail), 0, z.tail);
         if (dead) b.add(dead + j * z.dead, flat(st.idx_dead), 0, z.dead);
-        if (pos) b.add_plain(st.idx_block_pos, pos + j * z.block_pos, z.block_pos);
+        if (pos) b.add_device(st.idx_block_pos, pos + j * z.block_pos, z.block_pos);
         if (dead && !c.ids.empty())   // the indexer's moving spare row is the dead key again
             b.add(dead + j * z.dead, flat(st.idx_pooled + (c.ids.size() / block) * (size_t) g.idx_key_dim), 0, z.dead);
     }
@@ -602,21 +653,29 @@ ConversationRestore conversation_wire_mount_device(const uint8_t* payload, uint6
                                                    const QsaState& draft, const WireExpect& expect,
                                                    SavedConversation& meta, WireDecoded& info, std::string& error) {
     using R = ConversationRestore;
+    PhaseClock phases;
     if (!payload || bytes < kWireHeaderRecordBytes) {
         pfail(error, "no payload, or one shorter than its header");
         return R::invalid;
     }
-    std::vector<uint8_t> head(kWireHeaderRecordBytes);
-    if (!cuda_ok(cudaMemcpy(head.data(), payload, head.size(), cudaMemcpyDefault), error, "header copy")) return R::invalid;
+    // the header and, in the same read, the record stream when it fits the first kRecordPrefix bytes (records
+    // run to a few KiB; a second read fetches a longer stream): one synchronous round trip to the payload's GPU
+    constexpr uint64_t kRecordPrefix = 64 * 1024;
+    std::vector<uint8_t> records((size_t) std::min<uint64_t>(bytes, kRecordPrefix));
+    if (!cuda_ok(cudaMemcpy(records.data(), payload, records.size(), cudaMemcpyDefault), error, "header copy"))
+        return R::invalid;
     WireHeaderRecord h{};
-    if (!conversation_wire_peek(head.data(), head.size(), h, error)) return R::invalid;
+    if (!conversation_wire_peek(records.data(), kWireHeaderRecordBytes, h, error)) return R::invalid;
     if (h.blob_pool_off < kWireHeaderRecordBytes || h.blob_pool_off > bytes || h.payload_bytes > bytes) {
         pfail(error, "the header's records or payload run past the " + std::to_string(bytes) + " device bytes");
         return R::invalid;
     }
-    std::vector<uint8_t> records((size_t) h.blob_pool_off);
-    if (!cuda_ok(cudaMemcpy(records.data(), payload, records.size(), cudaMemcpyDefault), error, "records copy"))
-        return R::invalid;
+    if (h.blob_pool_off > records.size()) {
+        records.resize((size_t) h.blob_pool_off);
+        if (!cuda_ok(cudaMemcpy(records.data(), payload, records.size(), cudaMemcpyDefault), error, "records copy"))
+            return R::invalid;
+    }
+    records.resize((size_t) h.blob_pool_off);
     RecordSource src(std::move(records), bytes);
     wire_detail::BlobTable blobs;
     if (!wire_detail::decode_shape(src, meta, info, expect, blobs, error)) return R::invalid;
@@ -634,21 +693,26 @@ ConversationRestore conversation_wire_mount_device(const uint8_t* payload, uint6
     const int main_dev = resolve(stages.main_device);
     const int draft_dev = stages.empty() ? main_dev : resolve(stages.draft_device);
     {
-        const DeviceScope on(main_dev);
-        if (!device_sync(error)) return R::transfer_failed;
-        MountBatch b;
-        for (size_t j = 0; j < owned_count(ss); ++j) mount_kv(meta.kv[j], payload, blobs, owned_layer(ss, j), g, upto, true, b);
-        mount_running(meta.live, payload, blobs, ss, g, b);
-        if (!b.run(main_dev, error)) return R::transfer_failed;
-    }
-    {
-        MountBatch b;
-        mount_kv(meta.kv.back(), payload, blobs, draft, g, upto, false, b);
+        // the main session's layers, its running state and - when it lives on the same device - the draft layer
+        // in one batch: one set of launches and one wait
+        {
+            const DeviceScope on(main_dev);
+            if (!device_sync(error)) return R::transfer_failed;
+        }
         if (draft_dev != main_dev) {
             const DeviceScope on(draft_dev);
             if (!device_sync(error)) return R::transfer_failed;
         }
-        if (!b.run(draft_dev, error)) return R::transfer_failed;
+        phases.mark_prepared();
+        MountBatch b, d;
+        for (size_t j = 0; j < owned_count(ss); ++j) mount_kv(meta.kv[j], payload, blobs, owned_layer(ss, j), g, upto, true, b);
+        mount_running(meta.live, payload, blobs, ss, g, b);
+        mount_kv(meta.kv.back(), payload, blobs, draft, g, upto, false, draft_dev == main_dev ? b : d);
+        if (!b.issue(main_dev, error)) return R::transfer_failed;
+        if (draft_dev != main_dev && !d.issue(draft_dev, error)) return R::transfer_failed;
+        phases.mark_enqueued();
+        if (!MountBatch::complete(main_dev, error)) return R::transfer_failed;
+        if (draft_dev != main_dev && !MountBatch::complete(draft_dev, error)) return R::transfer_failed;
     }
     const size_t n = meta.live.ids.size();
     ss.ple_prev[0] = n >= 2 ? meta.live.ids[n - 2] : -1;
@@ -669,8 +733,11 @@ ConversationRestore conversation_wire_mount_device(const uint8_t* payload, uint6
         stage.session->ple_prev[0] = n >= 2 ? meta.live.ids[n - 2] : -1;
         stage.session->ple_prev[1] = n >= 1 ? meta.live.ids[n - 1] : -1;
     }
+    phases.finish();
     return R::restored;
 }
+
+WireDevicePhases conversation_wire_device_last_phases() { return t_last_phases; }
 
 ConversationRestore conversation_wire_mount_device(const uint8_t* payload, uint64_t bytes, SessionState& ss,
                                                    const ModelGeometry& g, const QsaState& draft,

@@ -649,36 +649,41 @@ int launch_copy_chained(const CopyPlan& plan, uint64_t total_tiles, const ChainA
 }
 
 namespace {
-constexpr int kZeroBatch = 256;
-struct ZeroRanges {
-    uint8_t* base;
+constexpr int kRangeBatch = 128;
+struct RangeBatch {
     int n;
-    uint32_t len[kZeroBatch];
-    uint64_t off[kZeroBatch];
+    uint32_t len[kRangeBatch];
+    uint8_t* dst[kRangeBatch];
+    const uint8_t* src[kRangeBatch];   // null: zero the range
 };
-/// One CTA per range (grid-stride over ranges): byte stores of zero.  For the few short pads of a payload.
-__global__ void zero_ranges_kernel(const __grid_constant__ ZeroRanges z) {
-    for (int r = blockIdx.x; r < z.n; r += gridDim.x)
-        for (uint32_t i = threadIdx.x; i < z.len[r]; i += blockDim.x) z.base[z.off[r] + i] = 0;
+/// One CTA per range (grid-stride over ranges), one byte per thread and step: the payload's alignment pads and its
+/// few sub-16-byte or unaligned pieces (the bulk engines move everything else).
+__global__ void byte_ranges_kernel(const __grid_constant__ RangeBatch b) {
+    for (int r = blockIdx.x; r < b.n; r += gridDim.x) {
+        uint8_t* d = b.dst[r];
+        const uint8_t* s = b.src[r];
+        for (uint32_t i = threadIdx.x; i < b.len[r]; i += blockDim.x) d[i] = s ? s[i] : uint8_t(0);
+    }
 }
 }  // namespace
 
-int zero_ranges(uint8_t* base, const std::vector<std::pair<uint64_t, uint64_t>>& ranges, cudaStream_t stream) {
-    ZeroRanges z;
-    z.base = base;
+int byte_ranges(const std::vector<ByteRange>& ranges, cudaStream_t stream) {
+    RangeBatch b;
     for (size_t i = 0; i < ranges.size();) {
-        z.n = 0;
-        for (; i < ranges.size() && z.n < kZeroBatch; ++i) {
-            if (ranges[i].second == 0) continue;
-            if (ranges[i].second > UINT32_MAX) return fail(SKV_EINVAL, "zero_ranges: a range above 4 GiB");
-            z.off[z.n] = ranges[i].first;
-            z.len[z.n] = (uint32_t) ranges[i].second;
-            ++z.n;
+        b.n = 0;
+        for (; i < ranges.size() && b.n < kRangeBatch; ++i) {
+            if (ranges[i].bytes == 0) continue;
+            if (ranges[i].bytes > kByteRangeMaxBytes)
+                return fail(SKV_EINVAL, "byte_ranges: a range above " + std::to_string(kByteRangeMaxBytes) + " bytes");
+            b.len[b.n] = (uint32_t) ranges[i].bytes;
+            b.dst[b.n] = ranges[i].dst;
+            b.src[b.n] = ranges[i].src;
+            ++b.n;
         }
-        if (!z.n) continue;
-        zero_ranges_kernel<<<std::min(z.n, 1024), 64, 0, stream>>>(z);
+        if (!b.n) continue;
+        byte_ranges_kernel<<<b.n, 128, 0, stream>>>(b);
         const cudaError_t e = cudaGetLastError();
-        if (e != cudaSuccess) return cuda_fail(e, "zero_ranges");
+        if (e != cudaSuccess) return cuda_fail(e, "byte_ranges");
     }
     return SKV_OK;
 }

@@ -115,8 +115,18 @@ int launch_copy_gated(const CopyPlan& plan, uint64_t total_tiles, const GateArgs
 /// Launch the chained TMA kernel (the counters are reset on `stream` first).
 int launch_copy_chained(const CopyPlan& plan, uint64_t total_tiles, const ChainArgs& chain, DeviceCtx& ctx,
                         cudaStream_t stream);
-/// Zero the byte ranges (offset, length) of `base` (device memory) on `stream`: the alignment pads of a payload.
-int zero_ranges(uint8_t* base, const std::vector<std::pair<uint64_t, uint64_t>>& ranges, cudaStream_t stream);
+/// A short byte range to write on the device: `bytes` from `src`, or zeros when `src` is null.  Both sides
+/// device-addressable (this GPU's memory, a peer's through P2P or CUDA IPC, or mapped pinned host memory).
+struct ByteRange {
+    uint8_t* dst;
+    const uint8_t* src;
+    uint64_t bytes;
+};
+/// The largest range byte_ranges takes: it is for pads and small unaligned pieces, not bulk data.
+constexpr uint64_t kByteRangeMaxBytes = 1u << 20;
+/// Write every range on `stream` in one launch per 128 ranges (byte loads and stores): a payload's alignment pads
+/// and the pieces too small or too unaligned for the bulk engines, instead of one copy-engine call each.
+int byte_ranges(const std::vector<ByteRange>& ranges, cudaStream_t stream);
 /// Enqueue the flag kernels.
 int launch_signal(uint64_t* flag, uint64_t value, cudaStream_t stream);
 int launch_wait(const uint64_t* flag, uint64_t value, uint64_t timeout_ns, uint32_t* status, cudaStream_t stream);

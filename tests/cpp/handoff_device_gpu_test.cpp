@@ -80,6 +80,7 @@ int prefill(const std::string& dir, int to_decode, int from_decode, pid_t decode
     uint8_t handle[64];
     check(skv_ipc_export(buf, handle) == SKV_OK, "payload exported through CUDA IPC");
     double publish_ms = 0, round_ms = 0;
+    WireDevicePhases pack{};
     WireEncoded enc;
     for (int round = 0; round < kRounds; ++round) {
         HandoffClaim claim;
@@ -89,6 +90,7 @@ int prefill(const std::string& dir, int to_decode, int from_decode, pid_t decode
                                         handle, 0, enc, err),
                  err, "the session packed into HBM and its descriptor published");
         publish_ms = ms_since(t0);
+        pack = conversation_wire_device_last_phases();
         check(enc.bytes == plan.total_bytes, "the published payload is the planned one");
         send_line(to_decode, "DONE " + std::to_string(claim.index) + " " + std::to_string(claim.nonce));
         const std::string ack = recv_line(from_decode, 120000);
@@ -103,6 +105,8 @@ int prefill(const std::string& dir, int to_decode, int from_decode, pid_t decode
     std::printf("prefill: last of %d rounds: publish (pack into HBM + descriptor) %.3f ms; fastest claim-to-release "
                 "(publish, DONE, decode mount, ACK, release) %.3f ms for %llu payload bytes; %d checks passed\n",
                 kRounds, publish_ms, round_ms, (unsigned long long) enc.bytes, checks);
+    std::printf("prefill: pack phases prepare %.3f issue %.3f complete %.3f total %.3f ms\n", pack.prepare_ms,
+                pack.issue_ms, pack.complete_ms, pack.total_ms);
     return 0;
 }
 
@@ -127,6 +131,7 @@ int decode(const std::string& dir, int from_prefill, int to_prefill) {
     SavedConversation meta;
     WireDecoded info;
     double mount_ms = 0;
+    WireDevicePhases mount{};
     unsigned long long nonce = 0;
     for (int round = 0; round < kRounds; ++round) {
         const std::string done = recv_line(from_prefill, 120000);
@@ -143,6 +148,7 @@ int decode(const std::string& dir, int from_prefill, int to_prefill) {
                   ConversationRestore::restored,
               ("mounted from GPU 0's HBM: " + err).c_str());
         mount_ms = ms_since(t0);
+        mount = conversation_wire_device_last_phases();
         if (round + 1 < kRounds) send_line(to_prefill, "ACK " + std::to_string(nonce));
     }
     for (size_t j = 0; j < c.qsa.size() + 1; ++j) {
@@ -163,6 +169,8 @@ int decode(const std::string& dir, int from_prefill, int to_prefill) {
     std::printf("decode: last of %d rounds: read the slot + mount from the peer's HBM %.3f ms (%llu payload bytes "
                 "over NVLink); %d checks passed\n",
                 kRounds, mount_ms, (unsigned long long) info.bytes, checks);
+    std::printf("decode: mount phases prepare %.3f issue %.3f complete %.3f total %.3f ms\n", mount.prepare_ms,
+                mount.issue_ms, mount.complete_ms, mount.total_ms);
     return 0;
 }
 
