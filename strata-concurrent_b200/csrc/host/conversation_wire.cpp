@@ -10,6 +10,7 @@
 #include "wire_detail.hpp"
 
 #include <algorithm>
+#include <bit>
 #include <cerrno>
 #include <cstdio>
 #include <cstring>
@@ -167,11 +168,18 @@ private:
         Bytes b;
         b.u64(c.ids.size());
         if (!out(b)) return false;
-        for (size_t i = 0; i < c.ids.size(); i += 4096) {   // ids go out in bounded pieces
-            Bytes piece;
-            const size_t n = std::min<size_t>(4096, c.ids.size() - i);
-            for (size_t j = 0; j < n; ++j) piece.u32((uint32_t) c.ids[i + j]);
-            if (!out(piece)) return false;
+        if constexpr (std::endian::native == std::endian::little) {
+            // the wire's little-endian int32 ids are the array's own bytes: emitted in place, no per-id work
+            if (!c.ids.empty() && !emit_(reinterpret_cast<const uint8_t*>(c.ids.data()), c.ids.size() * 4))
+                return false;
+        } else {
+            Bytes piece;   // ids go out in bounded pieces, each sized once and filled in one pass
+            for (size_t i = 0; i < c.ids.size(); i += 4096) {
+                const size_t n = std::min<size_t>(4096, c.ids.size() - i);
+                piece.b.resize(4 * n);
+                for (size_t j = 0; j < n; ++j) le32(piece.b.data() + 4 * j, (uint32_t) c.ids[i + j]);
+                if (!out(piece)) return false;
+            }
         }
         Bytes tail;
         if ((c.ids.size() * 4) % 8) tail.u32(0);

@@ -658,9 +658,10 @@ ConversationRestore conversation_wire_mount_device(const uint8_t* payload, uint6
         pfail(error, "no payload, or one shorter than its header");
         return R::invalid;
     }
-    // the header and, in the same read, the record stream when it fits the first kRecordPrefix bytes (records
-    // run to a few KiB; a second read fetches a longer stream): one synchronous round trip to the payload's GPU
-    constexpr uint64_t kRecordPrefix = 64 * 1024;
+    // the header and, in the same read, the record stream when it fits the first kRecordPrefix bytes (the records
+    // are a few KiB plus 4 bytes per token id: a 32K session's fit; a second read fetches a longer stream), so a
+    // mount makes one synchronous round trip to the payload's GPU
+    constexpr uint64_t kRecordPrefix = 256 * 1024;
     std::vector<uint8_t> records((size_t) std::min<uint64_t>(bytes, kRecordPrefix));
     if (!cuda_ok(cudaMemcpy(records.data(), payload, records.size(), cudaMemcpyDefault), error, "header copy"))
         return R::invalid;
