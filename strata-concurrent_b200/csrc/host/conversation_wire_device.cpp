@@ -12,6 +12,7 @@
 //    run of consecutive pieces; host-resident pieces are copied on the host, sub-16-byte pieces by the copy
 //    engine, and every byte of the pool nobody wrote is zeroed.
 #include "strata_kv/conversation_wire_device.hpp"
+#include "strata_kv/pinned.hpp"
 
 #include "kv_stream_detail.h"
 #include "skv_internal.h"
@@ -26,7 +27,9 @@
 #include <cstring>
 #include <functional>
 #include <map>
+#include <memory>
 #include <unordered_map>
+#include <utility>
 
 namespace strata::core {
 namespace {
@@ -460,25 +463,72 @@ bool conversation_wire_pack_device(const ConversationView& view, const SessionSt
 
 namespace {
 
-/// The records of a device payload, served from a host copy of [0, blob_pool_off); size() is the whole payload's.
+/// A page-locked host block from the recycling pool (strata_kv/pinned.hpp): device-to-host copies into it run at
+/// PCIe speed with no staging.
+struct PinnedBlock {
+    uint8_t* p = nullptr;
+    size_t n = 0;
+    explicit PinnedBlock(size_t bytes) : p(static_cast<uint8_t*>(strata::kv::pinned_alloc(bytes))), n(bytes) {}
+    PinnedBlock(PinnedBlock&& o) noexcept : p(std::exchange(o.p, nullptr)), n(std::exchange(o.n, 0)) {}
+    PinnedBlock(const PinnedBlock&) = delete;
+    PinnedBlock& operator=(const PinnedBlock&) = delete;
+    PinnedBlock& operator=(PinnedBlock&&) = delete;
+    ~PinnedBlock() {
+        if (p) strata::kv::pinned_free(p, n);
+    }
+};
+
+/// The records of a device payload, served from a host copy of [0, records); size() is the whole payload's.
 class RecordSource final : public WireSource {
 public:
-    RecordSource(std::vector<uint8_t> records, uint64_t total) : rec_(std::move(records)), total_(total) {}
+    RecordSource(PinnedBlock block, uint64_t records, uint64_t total)
+        : block_(std::move(block)), records_(records), total_(total) {}
     uint64_t size() const override { return total_; }
     bool read(uint8_t* dst, uint64_t offset, size_t bytes) const override {
-        if (offset > rec_.size() || bytes > rec_.size() - offset) return false;
-        std::memcpy(dst, rec_.data() + offset, bytes);
+        if (offset > records_ || bytes > records_ - offset) return false;
+        std::memcpy(dst, block_.p + offset, bytes);
         return true;
     }
     const uint8_t* span(uint64_t offset, size_t bytes) const override {
-        if (offset > rec_.size() || bytes > rec_.size() - offset) return nullptr;
-        return rec_.data() + offset;
+        if (offset > records_ || bytes > records_ - offset) return nullptr;
+        return block_.p + offset;
     }
 
 private:
-    std::vector<uint8_t> rec_;
+    PinnedBlock block_;
+    uint64_t records_;
     uint64_t total_;
 };
+
+/// The header and record stream of a device payload in one page-locked host block: a first read of
+/// kRecordPrefix bytes (the records are a few KiB plus 4 bytes per token id, so most sessions' fit), and a second
+/// read of only the rest when they run longer.  Null (and `error` set) on a refusal or a failed copy.
+constexpr uint64_t kRecordPrefix = 64 * 1024;
+std::unique_ptr<RecordSource> read_records(const uint8_t* payload, uint64_t bytes, std::string& error) {
+    try {
+        const uint64_t first = std::min<uint64_t>(bytes, kRecordPrefix);
+        PinnedBlock block(kRecordPrefix);
+        if (!cuda_ok(cudaMemcpy(block.p, payload, first, cudaMemcpyDefault), error, "header copy")) return nullptr;
+        WireHeaderRecord h{};
+        if (!conversation_wire_peek(block.p, kWireHeaderRecordBytes, h, error)) return nullptr;
+        if (h.blob_pool_off < kWireHeaderRecordBytes || h.blob_pool_off > bytes || h.payload_bytes > bytes) {
+            pfail(error, "the header's records or payload run past the " + std::to_string(bytes) + " device bytes");
+            return nullptr;
+        }
+        if (h.blob_pool_off > first) {
+            PinnedBlock whole((size_t) h.blob_pool_off);
+            std::memcpy(whole.p, block.p, (size_t) first);
+            if (!cuda_ok(cudaMemcpy(whole.p + first, payload + first, h.blob_pool_off - first, cudaMemcpyDefault),
+                         error, "records copy"))
+                return nullptr;
+            return std::make_unique<RecordSource>(std::move(whole), h.blob_pool_off, bytes);
+        }
+        return std::make_unique<RecordSource>(std::move(block), h.blob_pool_off, bytes);
+    } catch (const std::bad_alloc&) {
+        pfail(error, "no host memory for the payload's records");
+        return nullptr;
+    }
+}
 
 /// One device's share of a mount: copy-kernel segments by engine, plain copies for what the kernels cannot take,
 /// and work that must follow the writes.
@@ -658,26 +708,9 @@ ConversationRestore conversation_wire_mount_device(const uint8_t* payload, uint6
         pfail(error, "no payload, or one shorter than its header");
         return R::invalid;
     }
-    // the header and, in the same read, the record stream when it fits the first kRecordPrefix bytes (the records
-    // are a few KiB plus 4 bytes per token id: a 32K session's fit; a second read fetches a longer stream), so a
-    // mount makes one synchronous round trip to the payload's GPU
-    constexpr uint64_t kRecordPrefix = 256 * 1024;
-    std::vector<uint8_t> records((size_t) std::min<uint64_t>(bytes, kRecordPrefix));
-    if (!cuda_ok(cudaMemcpy(records.data(), payload, records.size(), cudaMemcpyDefault), error, "header copy"))
-        return R::invalid;
-    WireHeaderRecord h{};
-    if (!conversation_wire_peek(records.data(), kWireHeaderRecordBytes, h, error)) return R::invalid;
-    if (h.blob_pool_off < kWireHeaderRecordBytes || h.blob_pool_off > bytes || h.payload_bytes > bytes) {
-        pfail(error, "the header's records or payload run past the " + std::to_string(bytes) + " device bytes");
-        return R::invalid;
-    }
-    if (h.blob_pool_off > records.size()) {
-        records.resize((size_t) h.blob_pool_off);
-        if (!cuda_ok(cudaMemcpy(records.data(), payload, records.size(), cudaMemcpyDefault), error, "records copy"))
-            return R::invalid;
-    }
-    records.resize((size_t) h.blob_pool_off);
-    RecordSource src(std::move(records), bytes);
+    const std::unique_ptr<RecordSource> records = read_records(payload, bytes, error);
+    if (!records) return R::invalid;
+    const RecordSource& src = *records;
     wire_detail::BlobTable blobs;
     if (!wire_detail::decode_shape(src, meta, info, expect, blobs, error)) return R::invalid;
     for (auto& c : meta.checkpoints)
