@@ -93,6 +93,8 @@ def parse():
     ap.add_argument("--relay-mb", type=int, default=RELAY_CHUNK_BYTES >> 20, help="N = 1 e2e relay: piece size")
     ap.add_argument("--relay-lanes", type=int, default=2, choices=[1, 2],
                     help="N = 1 e2e relay: streams per direction the pieces alternate over")
+    ap.add_argument("--relay-ramp", default="off", choices=["on", "off"],
+                    help="N = 1 e2e relay: graded pieces at both ends of the stream (on) or per-segment pieces (off)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-length-sweep", action="store_true",
                     help="N = 1: leave out the 1K / 4K / 128K pool->pool lines the headline line carries")
@@ -342,24 +344,48 @@ def pcie_probe(torch, nbytes: int = 1 << 30, reps: int = 5) -> dict:
 RELAY_CHUNK_BYTES = 32 << 20
 
 
-def relay_pieces(park_segs: list, resume_segs: list, piece_bytes: int = RELAY_CHUNK_BYTES) -> list:
-    """A pipelined host relay's chunks: every park segment and its resume twin cut into the same pieces of at most
-    `piece_bytes`, as (park piece, resume piece) pairs in order."""
+def relay_pieces(park_segs: list, resume_segs: list, piece_bytes: int = RELAY_CHUNK_BYTES, ramp: bool = False) -> list:
+    """A pipelined host relay's pieces, as (park segments, resume segments) pairs in order.  Without `ramp`: every
+    park segment and its resume twin cut into the same pieces of at most `piece_bytes`.  With `ramp`: the whole
+    byte stream (the segments back to back) cut at graded points - pieces of 1/16, 1/16, 1/8, 1/4 and 1/2 of
+    `piece_bytes` at the start, whole pieces in the middle, the same ramp reversed at the end - so the resume
+    direction starts after a small first piece and the park direction's last piece is small too (the pipeline's
+    fill and drain), and no piece is a segment's short leftover."""
+    if not ramp:
+        return [([p], [r]) for ps, rs in zip(park_segs, resume_segs)
+                for p, r in zip(skv.split_segment(ps, piece_bytes), skv.split_segment(rs, piece_bytes))]
+    total = sum(sg.bytes for sg in park_segs)
+    steps = [piece_bytes // 16, piece_bytes // 16, piece_bytes // 8, piece_bytes // 4, piece_bytes // 2]
+    head, cuts, at = [], [0], 0
+    for n in steps:
+        at += n
+        head.append(at)
+    if 2 * head[-1] >= total:     # too short to ramp both ways: whole pieces only
+        cuts += list(range(piece_bytes, total, piece_bytes))
+    else:
+        tail = [total - c for c in reversed(head)]
+        span = tail[0] - head[-1]                       # the middle, in equal pieces of at most piece_bytes
+        n = -(-span // piece_bytes)
+        cuts += head + [head[-1] + (span * i // n) // 65536 * 65536 for i in range(1, n)] + tail
+    cuts.append(total)
     out = []
-    for p, r in zip(park_segs, resume_segs):
-        out += list(zip(skv.split_segment(p, piece_bytes), skv.split_segment(r, piece_bytes)))
+    for a, b in zip(cuts, cuts[1:]):
+        pp, rp = skv.slice_segments(park_segs, a, b), skv.slice_segments(resume_segs, a, b)
+        if pp:
+            out.append((pp, rp))
     return out
 
 
 def e2e_park_resume(torch, kg, src: SeqOnGpu, dst: SeqOnGpu, steps: int, warmup: int, side_steps: int,
-                    piece_bytes: int = RELAY_CHUNK_BYTES, lanes: int = 1) -> dict:
+                    piece_bytes: int = RELAY_CHUNK_BYTES, lanes: int = 1, ramp: bool = False) -> dict:
     """Host-mediated handoff through the C ABI: park to pinned host, resume into another table.
 
     relay (the reported e2e, fixed in advance): skv_park and skv_resume chunk by chunk on two streams - the park
            of chunk c+1 (device -> host) runs while the resume of chunk c (host -> device) runs, so both PCIe
            directions are busy at once.  Timed over `steps` steps.  lanes = 2 alternates the pieces over two
            streams per direction, so piece c+1's gather kernel runs beside piece c's device-to-host copy (and piece
-           c's scatter beside piece c+1's host-to-device copy) instead of holding the copy engine idle.
+           c's scatter beside piece c+1's host-to-device copy) instead of holding the copy engine idle.  ramp: graded
+           pieces at both ends of the stream (relay_pieces).
     staged / direct (extra keys): one skv_park then one skv_resume of the whole sequence, staged through device
            memory or with the kernel reading and writing mapped host memory.  Timed over `side_steps` steps."""
     off = skv.image_offsets(kg, src.tokens, kg.n_qsa)
@@ -372,12 +398,12 @@ def e2e_park_resume(torch, kg, src: SeqOnGpu, dst: SeqOnGpu, steps: int, warmup:
     resume_streams = [side] + [torch.cuda.Stream() for _ in range(lanes - 1)]
     park_segs = skv.pack_segments(src.ps, host.ptr)
     resume_segs = skv.unpack_segments(host.ptr, dst.ps)
-    chunks = relay_pieces(park_segs, resume_segs, piece_bytes)
+    chunks = relay_pieces(park_segs, resume_segs, piece_bytes, ramp)
     chunk_off = []
     at = 0
     for pp, _ in chunks:
         chunk_off.append(at)
-        at += (pp.bytes + 255) & ~255
+        at += sum((sg.bytes + 255) & ~255 for sg in pp)
     parked = [torch.cuda.Event() for _ in chunks]
     resumed = [torch.cuda.Event() for _ in resume_streams]
     parity, modes, results = {}, {}, {}
@@ -391,11 +417,11 @@ def e2e_park_resume(torch, kg, src: SeqOnGpu, dst: SeqOnGpu, steps: int, warmup:
                 for k, (pp, rp) in enumerate(chunks):
                     ps, rs = park_streams[k % lanes], resume_streams[k % lanes]
                     a = staging.data_ptr() + chunk_off[k]
-                    skv.park([pp], mode, a, staging.numel() - chunk_off[k], ps)
+                    skv.park(pp, mode, a, staging.numel() - chunk_off[k], ps)
                     parked[k].record(ps)
                     rs.wait_event(parked[k])
                     b2 = staging_b.data_ptr() + chunk_off[k]
-                    skv.resume([rp], mode, b2, staging_b.numel() - chunk_off[k], rs)
+                    skv.resume(rp, mode, b2, staging_b.numel() - chunk_off[k], rs)
                 for ev_r, rs in zip(resumed, resume_streams):
                     ev_r.record(rs)
                     stream.wait_event(ev_r)
@@ -417,10 +443,12 @@ def e2e_park_resume(torch, kg, src: SeqOnGpu, dst: SeqOnGpu, steps: int, warmup:
     host.close()
     r = results["relay"]
     return {"value": round(r["value"], 3), "unit": UNIT, "h2d_bytes_per_step": b, "d2h_bytes_per_step": b,
-            "mode": "relay", "piece_mb": piece_bytes >> 20, "lanes": lanes, "steps": r["steps"], "p50_ms": round(r["p50_ms"], 3), "p99_ms": round(r["p99_ms"], 3),
+            "mode": "relay", "piece_mb": piece_bytes >> 20, "lanes": lanes, "ramp": ramp, "pieces": len(chunks),
+            "steps": r["steps"], "p50_ms": round(r["p50_ms"], 3), "p99_ms": round(r["p99_ms"], 3),
             "pcie_gbs_both_directions": round(r["pcie_gbs_both_directions"], 3),
             "other_modes_gbs": {k: v for k, v in modes.items() if k != "relay"}, "other_modes_steps": side_steps,
-            "api": "skv_park + skv_resume (C ABI), pinned host image, 32 MB pieces on two streams",
+            "api": f"skv_park + skv_resume (C ABI), pinned host image, {piece_bytes >> 20} MB pieces"
+                   f"{' (graded at both ends)' if ramp else ''} over {lanes} stream(s) per direction",
             "parity": parity["relay"], "parity_by_mode": parity}
 
 
@@ -653,7 +681,7 @@ def run_single(args, torch) -> None:
                                 for n in SWEEP_TOKENS if n != t]
     if not args.no_e2e:
         e2e = e2e_park_resume(torch, kg, src, dst, args.steps, max(3, args.warmup), max(3, args.steps // 4),
-                              args.relay_mb << 20, args.relay_lanes)
+                              args.relay_mb << 20, args.relay_lanes, args.relay_ramp == "on")
         pcie = pcie_probe(torch)
         e2e["pcie_peak"] = pcie
         # the relay keeps both directions busy, so its bound is the two-direction probe

@@ -33,9 +33,11 @@ def test_state_layout():
         assert lay["flag"] + 8 <= lay["bytes"] and lay["bytes"] % 1024 == 0
 
 
-def test_relay_pieces_pair_park_and_resume_byte_for_byte():
-    """The e2e relay cuts every park segment and its resume twin at the same places: piece k of the park writes
-    exactly the host bytes piece k of the resume reads, and together they cover the whole image."""
+@pytest.mark.parametrize("ramp", [False, True])
+def test_relay_pieces_pair_park_and_resume_byte_for_byte(ramp):
+    """The e2e relay cuts the park segments and their resume twins at the same places: piece k of the park writes
+    exactly the host bytes piece k of the resume reads, and together they cover the whole image in order.  With the
+    ramp, the first and last pieces grade from 1/16 of a piece up and back down."""
     kg = skv.KvGeometry()
     t = 32768 + 5
 
@@ -46,14 +48,24 @@ def test_relay_pieces_pair_park_and_resume_byte_for_byte():
     host = 5 << 40
     park = skv.pack_segments(src, host)
     resume = skv.unpack_segments(host, src)
-    pieces = bench.relay_pieces(park, resume)
+    pieces = bench.relay_pieces(park, resume, ramp=ramp)
     assert len(pieces) > len(park)
-    covered = 0
-    for p, r in pieces:
-        assert p.bytes == r.bytes and p.bytes <= bench.RELAY_CHUNK_BYTES
-        assert p.dst == r.src                   # the park piece's host range is the resume piece's host range
-        covered += p.bytes
+    covered, host_at, sizes = 0, [], []
+    for pp, rp in pieces:
+        assert len(pp) == len(rp)
+        for p, r in zip(pp, rp):
+            assert p.bytes == r.bytes
+            assert p.dst == r.src               # the park piece's host range is the resume piece's host range
+            host_at.append((p.dst, p.bytes))
+        sizes.append(sum(p.bytes for p in pp))
+        assert sizes[-1] <= bench.RELAY_CHUNK_BYTES
+        covered += sizes[-1]
     assert covered == sum(s.bytes for s in park)
+    # the host image is written front to back: each piece starts where the previous one ended or at a new segment
+    assert len(set(host_at)) == len(host_at)
+    if ramp:
+        unit = bench.RELAY_CHUNK_BYTES // 16
+        assert sizes[:5] == [unit, unit, 2 * unit, 4 * unit, 8 * unit] and sizes[-5:] == sizes[:5][::-1]
 
 
 def test_mixed_plan_is_seeded_and_log_uniform():
