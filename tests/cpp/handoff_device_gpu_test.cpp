@@ -160,6 +160,7 @@ int decode(const std::string& dir, int from_prefill, int to_prefill) {
         const QsaState& st = c.qsa[j];
         check(from_device(st.idx_tail, content.tail[j].size()) == content.tail[j], "indexer tail arrived");
         check(from_device(st.idx_dead, content.dead[j].size()) == content.dead[j], "indexer dead key arrived");
+        check(from_device(st.idx_block_pos, 1)[0] == content.block_pos[j], "indexer block position arrived");
         const size_t rows = (size_t) (T / 4), dim = (size_t) g.idx_key_dim;
         const auto pooled = from_device(st.idx_pooled, (rows + 1) * dim);
         check(std::equal(pooled.begin(), pooled.begin() + rows * dim, content.pooled[j].begin()), "pooled rows arrived");
