@@ -1542,6 +1542,37 @@ class SeqSet:
                                   tables, state_base + self.offs[i], state_base + self.offs[i] + lay["ids"])
 
 
+HANDOVER_WAIT_NS = 5_000_000_000   # every config-5 hand-over wait ends by itself after 5 s of device time
+
+
+def issue_phase_run(L, arrays: list, wait, done, value: int, sp, gated: bool, on_start, on_end) -> None:
+    """Enqueue one run of config 5's phased order on stream `sp`: its copy launches (one per (segment array, count)
+    in `arrays`) after the hand-over it waits for (`wait`: a flag address, or None) and before the one it releases
+    (`done`, or None), both at `value`.  launch: skv_wait_flag, the copies and skv_signal are launches of their own;
+    gated: the wait rides in the first copy launch and the release in the last (skv_copy_gated), so a one-array run
+    is a single launch.  on_start / on_end record the run's timing events around its copies (with gated hand-overs
+    the wait falls between them)."""
+    if gated:
+        on_start()
+        last = len(arrays) - 1
+        for q, (arr, n) in enumerate(arrays):
+            w, d = (wait if q == 0 else None), (done if q == last else None)
+            if w is None and d is None:
+                skv.check(L.skv_copy(arr, n, skv.COPY_TMA, sp))
+            else:
+                skv.check(L.skv_copy_gated(arr, n, w, value, HANDOVER_WAIT_NS, d, value, sp))
+        on_end()
+        return
+    if wait is not None:
+        skv.check(L.skv_wait_flag(wait, value, HANDOVER_WAIT_NS, sp))
+    on_start()
+    for arr, n in arrays:
+        skv.check(L.skv_copy(arr, n, skv.COPY_TMA, sp))
+    on_end()
+    if done is not None:
+        skv.check(L.skv_signal(done, value, sp))
+
+
 def run_mixed(args, torch, probe: dict | None = None) -> dict | None:
     """Config 5: the even ranks prefill, the odd ranks decode.  64 sequences with seeded log-uniform lengths on
     [1K, 128K] live in their prefill owner's pool; each decode GPU pulls the sequences assigned to it (random
@@ -1672,26 +1703,8 @@ def run_mixed(args, torch, probe: dict | None = None) -> dict | None:
                     continue
                 wait = flags.base + 8 * run["wait"] if run["wait"] is not None else None
                 done = peer_flags[run["signal"][0]] + 8 * run["signal"][1] if run["signal"] is not None else None
-                if gated:
-                    # the wait inside the run's first launch, the release inside its last (skv_copy_gated)
-                    a.record(stream)
-                    last = len(run["arrays"]) - 1
-                    for q, (arr, n) in enumerate(run["arrays"]):
-                        w, d = (wait if q == 0 else None), (done if q == last else None)
-                        if w is None and d is None:
-                            skv.check(L.skv_copy(arr, n, skv.COPY_TMA, sp))
-                        else:
-                            skv.check(L.skv_copy_gated(arr, n, w, it + 1, 5_000_000_000, d, it + 1, sp))
-                    b.record(stream)
-                    continue
-                if wait is not None:
-                    skv.check(L.skv_wait_flag(wait, it + 1, 5_000_000_000, sp))
-                a.record(stream)
-                for arr, n in run["arrays"]:
-                    skv.check(L.skv_copy(arr, n, skv.COPY_TMA, sp))
-                b.record(stream)
-                if done is not None:
-                    skv.check(L.skv_signal(done, it + 1, sp))
+                issue_phase_run(L, run["arrays"], wait, done, it + 1, sp, gated,
+                                lambda: a.record(stream), lambda: b.record(stream))
             for st in tail_streams:
                 stream.wait_stream(st)
             first = {i: rev[j][0] for j in reversed(range(len(runs))) for i in runs[j]["starts"]}

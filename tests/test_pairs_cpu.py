@@ -362,3 +362,49 @@ def test_tail_phases_are_a_suffix_no_exclusive_run_waits_on(world, seed):
                 assert releaser[(d, r["wait"])] < r["phase"]
                 if r["phase"] < start:
                     assert releaser[(d, r["wait"])] < start
+
+
+class _RecordingLib:
+    """Stands in for the C ABI: records every launch call and succeeds."""
+
+    def __init__(self):
+        self.calls = []
+
+    def __getattr__(self, name):
+        def call(*a):
+            self.calls.append((name, a))
+            return 0
+        return call
+
+
+@pytest.mark.parametrize("gated", [False, True])
+@pytest.mark.parametrize("n_arrays", [1, 2, 3])
+@pytest.mark.parametrize("wait,done", [(None, None), (0x1000, None), (None, 0x2000), (0x1000, 0x2000)])
+def test_phase_run_launches(gated, n_arrays, wait, done):
+    """A config-5 run waits for its hand-over before its first byte moves and releases the next reader only after
+    its last copy: as launches of their own around the copies, or (gated) inside the first and last copy launch.
+    Every array is copied exactly once, in order, on the run's stream, with the step's flag value."""
+    L, marks = _RecordingLib(), []
+    arrays = [(f"arr{q}", 10 + q) for q in range(n_arrays)]
+    bench.issue_phase_run(L, arrays, wait, done, 7, "sp", gated, lambda: marks.append(len(L.calls)),
+                          lambda: marks.append(len(L.calls)))
+    names = [c[0] for c in L.calls]
+    copied = [c[1][0] for c in L.calls if c[0] in ("skv_copy", "skv_copy_gated")]
+    assert copied == [a for a, _ in arrays]
+    assert all(c[1][-1] == "sp" for c in L.calls)
+    if gated:
+        assert "skv_wait_flag" not in names and "skv_signal" not in names
+        gates = [(c[1][2], c[1][5]) for c in L.calls if c[0] == "skv_copy_gated"]
+        expect = [(wait if q == 0 else None, done if q == n_arrays - 1 else None) for q in range(n_arrays)]
+        assert gates == [g for g in expect if g != (None, None)]
+        assert all(c[1][3] == 7 and c[1][6] == 7 and c[1][4] == bench.HANDOVER_WAIT_NS
+                   for c in L.calls if c[0] == "skv_copy_gated")
+        assert len(L.calls) == n_arrays and marks == [0, n_arrays]
+    else:
+        assert "skv_copy_gated" not in names
+        assert names == (["skv_wait_flag"] if wait else []) + ["skv_copy"] * n_arrays + (["skv_signal"] if done else [])
+        if wait:
+            assert L.calls[0][1] == (wait, 7, bench.HANDOVER_WAIT_NS, "sp")
+        if done:
+            assert L.calls[-1][1] == (done, 7, "sp")
+        assert marks == [int(bool(wait)), int(bool(wait)) + n_arrays]
