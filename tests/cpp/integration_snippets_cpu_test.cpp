@@ -66,6 +66,19 @@ void phased(const uint64_t* bytes_pre_to_dec, int n_pre, int n_dec, int me, cons
     int n_pieces = 0;
     for (int j = 0; j < n_runs[(size_t) me]; ++j) {
         const skv_sched_run& r = runs[(size_t) (me * max_runs + j)];
+        skv_slice_segments(flow[r.src], n_flow[r.src], r.lo, r.hi, pieces, 64, &n_pieces);
+        skv_copy_gated(pieces, n_pieces, r.wait >= 0 ? &my_flags[r.wait] : nullptr, step, 2'000'000'000,
+                       r.signal_dst >= 0 ? &peer_flags[r.signal_dst][r.signal_idx] : nullptr, step, stream);
+    }
+}
+
+// 3, the same with the hand-overs as launches of their own
+void phased_launches(const skv_sched_run* runs, int n, const skv_segment* const* flow, const int* n_flow,
+                     uint64_t* my_flags, uint64_t* const* peer_flags, uint64_t step, void* stream) {
+    skv_segment pieces[64];
+    int n_pieces = 0;
+    for (int j = 0; j < n; ++j) {
+        const skv_sched_run& r = runs[j];
         if (r.wait >= 0) skv_wait_flag(&my_flags[r.wait], step, 2'000'000'000, stream);
         skv_slice_segments(flow[r.src], n_flow[r.src], r.lo, r.hi, pieces, 64, &n_pieces);
         skv_copy(pieces, n_pieces, SKV_COPY_TMA, stream);
