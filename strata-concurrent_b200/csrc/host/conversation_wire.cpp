@@ -776,7 +776,8 @@ private:
             return refuse(error_, "a checkpoint's id count " + num(n_ids) + " does not fit its record");
         c.ids.resize((size_t) n_ids);
         if (!field(pos, end, c.ids.data(), (size_t) n_ids * 4, "CHECKPOINT")) return false;
-        for (auto& id : c.ids) id = (int32_t) rd32(reinterpret_cast<const uint8_t*>(&id));
+        if constexpr (std::endian::native != std::endian::little)   // the wire's int32s are little-endian
+            for (auto& id : c.ids) id = (int32_t) rd32(reinterpret_cast<const uint8_t*>(&id));
         if ((n_ids * 4) % 8) {
             uint8_t pad[4];
             if (!field(pos, end, pad, 4, "CHECKPOINT")) return false;
